@@ -1,0 +1,258 @@
+// C ABI of the library (include/apsi_lowbit.h): argument checks, device setup, dispatch.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <atomic>
+#include <mutex>
+
+#include "../../include/apsi_lowbit.h"
+#include "lb_common.cuh"
+#include "lb_kernels.h"
+
+namespace lb {
+namespace {
+thread_local char t_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+struct DevInfo {
+  std::atomic<int> ready{0};
+  int sms = 0, l2 = 0, major = 0, minor = 0;
+};
+DevInfo g_dev[64];
+std::mutex g_init_mu;
+
+int init_device(int dev, DevInfo** out) {
+  if (dev < 0 || dev >= 64) return fail(LB_E_DEVICE, "device %d out of range", dev);
+  DevInfo& d = g_dev[dev];
+  if (!d.ready.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (!d.ready.load(std::memory_order_relaxed)) {
+      cudaDeviceProp prop;
+      cudaError_t e = cudaGetDeviceProperties(&prop, dev);
+      if (e != cudaSuccess) return fail(LB_E_DEVICE, "cudaGetDeviceProperties(%d): %s", dev, cudaGetErrorString(e));
+      if (prop.major != 10)
+        return fail(LB_E_DEVICE, "device %d is compute capability %d.%d; this library is built for sm_100a only",
+                    dev, prop.major, prop.minor);
+      d.sms = prop.multiProcessorCount;
+      d.l2 = prop.l2CacheSize;
+      d.major = prop.major;
+      d.minor = prop.minor;
+      d.ready.store(1, std::memory_order_release);
+    }
+  }
+  *out = &d;
+  return LB_OK;
+}
+
+int current(DevInfo** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(LB_E_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+  return init_device(dev, out);
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int launched(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(LB_E_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  t_err[0] = 0;
+  return LB_OK;
+}
+
+int check_weight_input(const void* w, int dt, int64_t N, int64_t K, int64_t kmult, const char* who) {
+  if (!w) return fail(LB_E_ARG, "%s: weight pointer is NULL", who);
+  if (dt != LB_DT_F32 && dt != LB_DT_BF16) return fail(LB_E_ARG, "%s: w_dtype must be LB_DT_F32 or LB_DT_BF16", who);
+  if (N <= 0 || K <= 0) return fail(LB_E_ARG, "%s: N and K must be positive (got %lld, %lld)", who, (long long)N, (long long)K);
+  if (K % kmult) return fail(LB_E_ARG, "%s: K (%lld) must be a multiple of %lld", who, (long long)K, (long long)kmult);
+  if (!aligned(w, 16)) return fail(LB_E_ALIGN, "%s: weight pointer must be 16-byte aligned", who);
+  return LB_OK;
+}
+}  // namespace
+
+// ------------------------------------------------------------------------------------------- interleave
+__global__ void interleave_kernel(const uint16_t* __restrict__ src, int G, int64_t M, int64_t Nl,
+                                  uint16_t* __restrict__ dst) {
+  const int64_t total = static_cast<int64_t>(G) * M * Nl;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t j = i % Nl;
+    const int64_t m = (i / Nl) % M;
+    const int64_t g = i / (Nl * M);
+    dst[m * (Nl * G) + g * Nl + j] = src[i];
+  }
+}
+
+cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(G) * M * Nl;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  interleave_kernel<<<static_cast<unsigned>(blocks > 0 ? blocks : 1), 256, 0, st>>>(
+      reinterpret_cast<const uint16_t*>(src), G, M, Nl, reinterpret_cast<uint16_t*>(dst));
+  return cudaGetLastError();
+}
+
+}  // namespace lb
+
+using namespace lb;
+
+extern "C" {
+
+int lb_version(void) { return LB_VERSION; }
+
+const char* lb_last_error(void) { return t_err; }
+
+int lb_init(int device) {
+  DevInfo* d;
+  return init_device(device, &d);
+}
+
+int lb_device_errors(void* stream, int* bits_out) {
+  if (!bits_out) return fail(LB_E_ARG, "lb_device_errors: bits_out is NULL");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(LB_E_DEVICE, "lb_device_errors: %s", cudaGetErrorString(e));
+  int v = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&v, g_dev_errors, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_dev_errors, &zero, sizeof(int));
+  if (e != cudaSuccess) return fail(LB_E_DEVICE, "lb_device_errors: %s", cudaGetErrorString(e));
+  *bits_out = v;
+  return LB_OK;
+}
+
+int lb_quant_int8_rows(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* codes, uint16_t* scale16,
+                       float* scale32, void* stream) {
+  int r = check_weight_input(w, w_dtype, N, K, 8, "lb_quant_int8_rows");
+  if (r) return r;
+  if (!codes || !scale16) return fail(LB_E_ARG, "lb_quant_int8_rows: codes and scale16 are required");
+  if (!aligned(codes, 8) || !aligned(scale16, 2) || (scale32 && !aligned(scale32, 4)))
+    return fail(LB_E_ALIGN, "lb_quant_int8_rows: codes must be 8-byte aligned");
+  DevInfo* d;
+  if ((r = current(&d))) return r;
+  return launched(launch_quant_int8_rows(w, w_dtype, N, K, codes, scale16, scale32, d->sms,
+                                         static_cast<cudaStream_t>(stream)),
+                  "quant_int8_rows");
+}
+
+int lb_quant_int4_g128(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* packed, uint16_t* scale16,
+                       float* scale32, void* stream) {
+  int r = check_weight_input(w, w_dtype, N, K, 128, "lb_quant_int4_g128");
+  if (r) return r;
+  if (!packed || !scale16) return fail(LB_E_ARG, "lb_quant_int4_g128: packed and scale16 are required");
+  if (!aligned(packed, 4) || !aligned(scale16, 2) || (scale32 && !aligned(scale32, 4)))
+    return fail(LB_E_ALIGN, "lb_quant_int4_g128: packed must be 4-byte aligned");
+  DevInfo* d;
+  if ((r = current(&d))) return r;
+  return launched(launch_quant_int4_g128(w, w_dtype, N, K, packed, scale16, scale32, d->sms,
+                                         static_cast<cudaStream_t>(stream)),
+                  "quant_int4_g128");
+}
+
+static int quant_g32(int kind, const void* w, int w_dtype, int64_t N, int64_t K, uint32_t* words, float* scale32,
+                     void* stream, const char* who) {
+  int r = check_weight_input(w, w_dtype, N, K, 32, who);
+  if (r) return r;
+  if (!words || !scale32) return fail(LB_E_ARG, "%s: words and scale32 are required", who);
+  if (!aligned(words, 8) || !aligned(scale32, 4)) return fail(LB_E_ALIGN, "%s: words must be 8-byte aligned", who);
+  DevInfo* d;
+  if ((r = current(&d))) return r;
+  return launched(launch_quant_g32(kind, w, w_dtype, N, K, words, scale32, d->sms, static_cast<cudaStream_t>(stream)),
+                  who);
+}
+
+int lb_quant_q8_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t* words, float* scale32,
+                      void* stream) {
+  return quant_g32(8, w, w_dtype, N, K, words, scale32, stream, "lb_quant_q8_0_g32");
+}
+
+int lb_quant_q4_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t* words, float* scale32,
+                      void* stream) {
+  return quant_g32(4, w, w_dtype, N, K, words, scale32, stream, "lb_quant_q4_0_g32");
+}
+
+int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, int64_t N, int64_t K, void* out,
+               int out_dtype, void* stream) {
+  if (fmt < LB_FMT_INT8_ROW || fmt > LB_FMT_Q4_0_G32) return fail(LB_E_ARG, "lb_dequant: unknown format %d", fmt);
+  if (!codes || !scales || !out) return fail(LB_E_ARG, "lb_dequant: NULL pointer");
+  if (out_dtype != LB_DT_F32 && out_dtype != LB_DT_BF16) return fail(LB_E_ARG, "lb_dequant: bad out_dtype");
+  if (scale_dtype != LB_DT_F32 && scale_dtype != LB_DT_F16) return fail(LB_E_ARG, "lb_dequant: bad scale_dtype");
+  if ((fmt == LB_FMT_Q8_0_G32 || fmt == LB_FMT_Q4_0_G32) && scale_dtype != LB_DT_F32)
+    return fail(LB_E_ARG, "lb_dequant: the g32 formats have float32 scales");
+  if (N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_dequant: N and K must be positive");
+  const int64_t kmult = fmt == LB_FMT_INT4_G128 ? 128 : (fmt == LB_FMT_INT8_ROW ? 8 : 32);
+  if (K % kmult) return fail(LB_E_ARG, "lb_dequant: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
+  if (!aligned(codes, 8) || !aligned(out, 16) || !aligned(scales, scale_dtype == LB_DT_F32 ? 4 : 2))
+    return fail(LB_E_ALIGN, "lb_dequant: codes 8-byte, out 16-byte, scales element aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_dequant(fmt, codes, scales, scale_dtype == LB_DT_F32 ? 1 : 0, N, K, out, out_dtype, d->sms,
+                                 static_cast<cudaStream_t>(stream)),
+                  "dequant");
+}
+
+static bool use_gemv(int64_t M) { return M <= 16; }
+
+int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes) {
+  if (!bytes) return fail(LB_E_ARG, "lb_linear_workspace_size: bytes is NULL");
+  if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
+    return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
+  if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_workspace_size: sizes must be positive");
+  *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
+  return LB_OK;
+}
+
+int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+              const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+              void* stream) {
+  if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
+    return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
+  if (!x || !codes || !scales || !y) return fail(LB_E_ARG, "lb_linear: x, codes, scales and y are required");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear: M, N, K must be positive");
+  if (M > (1LL << 31) || N > (1LL << 31)) return fail(LB_E_ARG, "lb_linear: M and N must be below 2^31");
+  const int64_t kmult = fmt == LB_FMT_INT4_G128 ? 128 : 64;
+  if (K % kmult) return fail(LB_E_ARG, "lb_linear: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
+  if (ldy < N) return fail(LB_E_ARG, "lb_linear: ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
+  if (!aligned(x, 16) || !aligned(codes, 16)) return fail(LB_E_ALIGN, "lb_linear: x and codes must be 16-byte aligned");
+  if (!aligned(y, 2) || !aligned(scales, 2) || (bias && !aligned(bias, 2)))
+    return fail(LB_E_ALIGN, "lb_linear: y, scales and bias must be 2-byte aligned");
+  if (use_gemv(M) && K > gemv_max_k(fmt))
+    return fail(LB_E_UNSUPPORTED, "lb_linear: K (%lld) above %d is not supported for M <= 16", (long long)K,
+                gemv_max_k(fmt));
+  size_t need = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
+  if (need) {
+    if (!workspace || ws_bytes < need)
+      return fail(LB_E_WORKSPACE, "lb_linear: workspace of %zu bytes needed (got %zu)", need, workspace ? ws_bytes : 0);
+    if (!aligned(workspace, 256)) return fail(LB_E_ALIGN, "lb_linear: workspace must be 256-byte aligned");
+  }
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_gemv(M))
+    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, st), "gemv");
+  const char* why = nullptr;
+  cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why);
+  if (e != cudaSuccess && why) return fail(LB_E_LAUNCH, "gemm: %s (%s)", why, cudaGetErrorString(e));
+  return launched(e, "gemm");
+}
+
+int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst, void* stream) {
+  if (!src || !dst) return fail(LB_E_ARG, "lb_interleave_cols: NULL pointer");
+  if (G <= 0 || M <= 0 || Nl <= 0) return fail(LB_E_ARG, "lb_interleave_cols: sizes must be positive");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_interleave(src, G, M, Nl, dst, static_cast<cudaStream_t>(stream)), "interleave");
+}
+
+}  // extern "C"

@@ -1,0 +1,453 @@
+// Prefill-regime product (M > 16 tokens) on the 5th-generation tensor cores (tcgen05).
+//
+//   D[n, m] = sum_k deq(W)[n, k] * x[m, k]      A = W tile (128 weight rows)   in TENSOR MEMORY
+//                                                B = x tile (BN tokens)         in shared memory (TMA, SW128)
+//                                                D = fp32 accumulators          in TENSOR MEMORY
+//
+// Why A lives in tensor memory: the weights arrive as 4/8-bit codes and must be expanded before the MMA.
+// Writing the expanded tile to shared memory and reading it back through the MMA would double the shared-
+// memory traffic of the weight operand on top of the activation stream; tcgen05.st puts it in TMEM instead,
+// so shared memory only carries the TMA-staged activations and the small raw code tiles.
+//
+// Operands are fp16: codes are exact in fp16 and int4 weights are fp16(q * s16) with a single rounding
+// (relative error <= 2^-11); the activations are converted once by prep_x_kernel with a per-row power-of-two
+// factor so the conversion is exact (bf16 mantissas fit in fp16) and cannot overflow; the factor is undone in
+// the epilogue.  int8 rows keep exact codes and apply the row scale in float32 in the epilogue.
+//
+// Roles (10 warps, persistent over tiles):
+//   warp 0      TMA producer: activation tile (BN x 64 fp16, SW128) + raw code tile (128 rows) per stage
+//   warp 1      TMEM allocator and MMA issuer (one thread): 4 x tcgen05.mma K=16 per stage, commit -> mbarrier
+//   warps 2..9  dequantise one quarter of the rows x one half of the stage's K into TMEM (tcgen05.st), then
+//               run the tile epilogue (tcgen05.ld -> scale -> bf16 -> global)
+// All mbarrier waits are bounded (lb::mbar_wait); a timeout sets the device error word and the CTA drains.
+#include <cuda.h>
+#include "lb_common.cuh"
+#include "lb_kernels.h"
+
+namespace lb {
+
+namespace gemm {
+constexpr int BM = 128;     // weight rows per tile = TMEM lanes
+constexpr int BK = 64;      // K values per stage
+constexpr int STAGES = 4;
+constexpr int THREADS = 320;
+}  // namespace gemm
+
+struct GemmParams {
+  const __half* s16;        // int4: [N, K/128]; int8: [N]
+  const uint16_t* bias;     // bf16 [N] or null
+  uint16_t* y;              // bf16 [M, ldy]
+  const float* tokscale;    // [M] power-of-two factors from prep_x_kernel
+  int64_t M, N, K, ldy;
+  int acc;
+  int m_blocks, n_blocks, tiles, ksteps;
+};
+
+template <int FMT>
+struct GemmCfg {
+  static constexpr int RAW_ROW = (FMT == 2) ? 32 : 64;       // code bytes of a row per stage
+  static constexpr int RAW_STAGE = gemm::BM * RAW_ROW;
+};
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int X_STAGE = BN * 128;
+  static constexpr int TMEM_COLS = (BN + gemm::STAGES * 32 <= 256) ? 256 : 512;
+};
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits_g(float f) {
+  __nv_bfloat16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// ------------------------------------------------------------------------------------------- activations
+// One warp per token row: absmax, power-of-two factor, K-permuted fp16 copy.
+// PERM 0 (int4 nibble pairs): position L of each 8-block takes x[8b + {0,4,1,5,2,6,3,7}[L]].
+// PERM 1 (int8 byte pairs):   position L of each 4-block takes x[4b + {0,2,1,3}[L]].
+template <int PERM>
+__global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K,
+                                                     uint16_t* __restrict__ x16, float* __restrict__ tokscale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const uint16_t* xr = x + row * K;
+  float m = 0.f;
+  for (int64_t k = lane * 8; k < K; k += 256) {
+    uint4 v = ldg_nc_v4(xr + k);
+    uint32_t r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m = fmaxf(m, fabsf(__uint_as_float(r[j] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(r[j] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int e = 0;
+  if (m > 0.f) {
+    int ex;
+    frexpf(m, &ex);           // m = f * 2^ex, f in [0.5, 1)
+    e = ex - 15;              // max |x| * 2^-e in [2^14, 2^15)
+    e = e < -110 ? -110 : (e > 110 ? 110 : e);
+  }
+  const float down = ldexpf(1.0f, -e);
+  if (lane == 0) tokscale[row] = ldexpf(1.0f, e);
+  uint16_t* out = x16 + row * K;
+  for (int64_t k = lane * 8; k < K; k += 256) {
+    uint4 v = ldg_nc_v4(xr + k);
+    uint32_t r[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] = __uint_as_float(r[j] << 16) * down;
+      f[2 * j + 1] = __uint_as_float(r[j] & 0xFFFF0000u) * down;
+    }
+    float g[8];
+    if (PERM == 0) {
+      g[0] = f[0]; g[1] = f[4]; g[2] = f[1]; g[3] = f[5]; g[4] = f[2]; g[5] = f[6]; g[6] = f[3]; g[7] = f[7];
+    } else {
+      g[0] = f[0]; g[1] = f[2]; g[2] = f[1]; g[3] = f[3]; g[4] = f[4]; g[5] = f[6]; g[6] = f[5]; g[7] = f[7];
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 h = __floats2half2_rn(g[2 * j], g[2 * j + 1]);
+      o[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + k) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------- dequantisers
+// int4: 16 bytes = 32 codes of one row (k = 8i + j for word i, nibble j) -> 16 fp16 pairs in logical K order
+// (pair 4i + p holds physical nibbles (p, p + 4) of word i), each fp16(q * s).
+__device__ __forceinline__ void deq_int4_f16(const uint4 raw, uint32_t s2, uint32_t (&o)[16]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t v = w[i];
+    const uint32_t v8 = v >> 8;
+    // 1024 + (q + 8) and 1024 + 16 (q + 8): offset-binary through the XOR folded into the LOP3
+    const uint32_t p0 = lop3_and_xor_or(v, 0x000F000Fu, 0x64086408u);
+    const uint32_t p1 = lop3_and_xor_or(v, 0x00F000F0u, 0x64806480u);
+    const uint32_t p2 = lop3_and_xor_or(v8, 0x000F000Fu, 0x64086408u);
+    const uint32_t p3 = lop3_and_xor_or(v8, 0x00F000F0u, 0x64806480u);
+    // exact codes: p0 - 1032 ; p1 / 16 - 72
+    const uint32_t q0 = h2_fma(p0, 0x3C003C00u, 0xE408E408u);
+    const uint32_t q1 = h2_fma(p1, 0x2C002C00u, 0xD480D480u);
+    const uint32_t q2 = h2_fma(p2, 0x3C003C00u, 0xE408E408u);
+    const uint32_t q3 = h2_fma(p3, 0x2C002C00u, 0xD480D480u);
+    o[4 * i + 0] = h2_mul(q0, s2);
+    o[4 * i + 1] = h2_mul(q1, s2);
+    o[4 * i + 2] = h2_mul(q2, s2);
+    o[4 * i + 3] = h2_mul(q3, s2);
+  }
+}
+// int8: 32 bytes of one row -> 16 fp16 pairs of exact codes; pair 2i holds bytes (0, 2), pair 2i+1 bytes
+// (1, 3) of word i.
+__device__ __forceinline__ void deq_int8_f16(const uint4 a, const uint4 b, uint32_t (&o)[16]) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t v = w[i] ^ 0x80808080u;                       // q + 128
+    const uint32_t p02 = prmt(v, 0x00006464u, 0x5240u);          // (1024 + n0, 1024 + n2)
+    const uint32_t p13 = prmt(v, 0x00006464u, 0x5341u);          // (1024 + n1, 1024 + n3)
+    o[2 * i] = h2_fma(p02, 0x3C003C00u, 0xE480E480u);            // - 1152
+    o[2 * i + 1] = h2_fma(p13, 0x3C003C00u, 0xE480E480u);
+  }
+}
+
+// ------------------------------------------------------------------------------------------- the GEMM
+template <int FMT, int BN>
+__global__ void __launch_bounds__(gemm::THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                const GemmParams p) {
+  using namespace gemm;
+  using Cfg = GemmCfg<FMT>;
+  using Sm = GemmSmem<BN>;
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];
+  // 1024-align the carve-out (SW128 atoms)
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
+  uint8_t* xs = smem;                                          // STAGES x X_STAGE
+  uint8_t* raw = xs + STAGES * Sm::X_STAGE;                    // STAGES x RAW_STAGE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + STAGES * Cfg::RAW_STAGE);
+  uint64_t* full_x = bars;
+  uint64_t* full_w = bars + STAGES;
+  uint64_t* a_full = bars + 2 * STAGES;
+  uint64_t* empty = bars + 3 * STAGES;
+  uint64_t* acc_full = bars + 4 * STAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_x[s], 1);
+      mbar_init(&full_w[s], 1);
+      mbar_init(&a_full[s], 8);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Sm::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  volatile int* abort_v = abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+        const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+        for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+          const uint32_t slot = it % STAGES;
+          if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
+          mbar_arrive_expect_tx(&full_x[slot], Sm::X_STAGE);
+          tma_load_2d(xs + slot * Sm::X_STAGE, &tm_x, ks * BK, nb * BN, &full_x[slot]);
+          mbar_arrive_expect_tx(&full_w[slot], Cfg::RAW_STAGE);
+          tma_load_2d(raw + slot * Cfg::RAW_STAGE, &tm_w, ks * Cfg::RAW_ROW, mb * BM, &full_w[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+      uint32_t it = 0, tcount = 0;
+      for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
+        if (tcount > 0) mbar_wait(acc_empty, (tcount - 1) & 1, abort_v);
+        tc_fence_after();
+        for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+          const uint32_t slot = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          mbar_wait(&full_x[slot], ph, abort_v);
+          mbar_wait(&a_full[slot], ph, abort_v);
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(xs + slot * Sm::X_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(xaddr + kk * 32);
+            const uint32_t a_tmem = tmem + BN + slot * 32 + kk * 8;
+            tc_mma_ts(tmem, a_tmem, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[slot]);
+        }
+        tc_commit(acc_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ dequantise + epilogue
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int h = (warp - 2) >> 2;          // K half of each stage
+    const int rloc = q * 32 + lane;         // row within the tile
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t it = 0, tcount = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
+      const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+      const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
+      const int64_t rowc = row < p.N ? row : p.N - 1;
+      for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+        const uint32_t slot = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        uint32_t s2 = 0;
+        if (FMT == 2) {
+          const __half s = p.s16[rowc * (p.K / 128) + (ks * BK) / 128];
+          const __half2 sp = __halves2half2(s, s);
+          s2 = *reinterpret_cast<const uint32_t*>(&sp);
+        }
+        mbar_wait(&full_w[slot], ph, abort_v);
+        if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
+        uint32_t o[16];
+        const uint32_t rbase = smem_u32(raw + slot * Cfg::RAW_STAGE) + rloc * Cfg::RAW_ROW;
+        if (FMT == 2) {
+          // SWIZZLE_32B: 16-byte chunk index ^= bit 7 of the offset (row >> 2)
+          const uint4 r = lds_v4(rbase + 16 * (h ^ ((rloc >> 2) & 1)));
+          deq_int4_f16(r, s2, o);
+        } else {
+          // SWIZZLE_64B: chunk index (0..3) ^= bits 7..8 of the offset (row >> 1)
+          const int sw = (rloc >> 1) & 3;
+          const uint4 a = lds_v4(rbase + 16 * ((2 * h) ^ sw));
+          const uint4 b = lds_v4(rbase + 16 * ((2 * h + 1) ^ sw));
+          deq_int8_f16(a, b, o);
+        }
+        tmem_st_x16(tmem + lane_addr + BN + slot * 32 + 16 * h, o);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[slot]);
+      }
+      // ---------------------------------------------------------------- epilogue of this tile
+      mbar_wait(acc_full, tcount & 1, abort_v);
+      tc_fence_after();
+      float rs = 1.f, bias = 0.f;
+      if (FMT == 1) rs = __half2float(p.s16[rowc]);
+      if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
+      const bool row_ok = row < p.N;
+#pragma unroll 1
+      for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 16) {
+        uint32_t d[16];
+        tmem_ld_x16(tmem + lane_addr + c0, d);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int64_t tok = static_cast<int64_t>(nb) * BN + c0 + j;
+          if (row_ok && tok < p.M) {
+            float v = __uint_as_float(d[j]) * (p.tokscale[tok] * rs);
+            v += bias;
+            uint16_t* yp = p.y + tok * p.ldy + row;
+            if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
+            *yp = f32_to_bf16_bits_g(v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Sm::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+  }
+  return fn;
+}
+
+static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
+
+size_t gemm_smem_bytes(int fmt, int bn) {
+  const int raw = (fmt == 2) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
+  return 1024 + static_cast<size_t>(gemm::STAGES) * (bn * 128 + raw) + 256;
+}
+
+size_t gemm_workspace_bytes(int64_t M, int64_t K) {
+  size_t x16 = static_cast<size_t>(M * K) * 2;
+  x16 = (x16 + 255) & ~static_cast<size_t>(255);
+  return x16 + static_cast<size_t>(M) * sizeof(float) + 256;
+}
+
+template <int FMT, int BN>
+static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int sms,
+                                 cudaStream_t st) {
+  const size_t smem = gemm_smem_bytes(FMT, BN);
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  const int grid = p.tiles < sms ? p.tiles : sms;
+  gemm_kernel<FMT, BN><<<grid, gemm::THREADS, smem, st>>>(tx, tw, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
+                        int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
+                        cudaStream_t st, const char** why) {
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) {
+    *why = "cuTensorMapEncodeTiled is not available from the driver";
+    return cudaErrorNotSupported;
+  }
+  // workspace: permuted fp16 activations + per-token factors
+  size_t x16b = static_cast<size_t>(M * K) * 2;
+  x16b = (x16b + 255) & ~static_cast<size_t>(255);
+  uint16_t* x16 = reinterpret_cast<uint16_t*>(ws);
+  float* tokscale = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + x16b);
+  {
+    const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
+    if (fmt == 2)
+      prep_x_kernel<0><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
+    else
+      prep_x_kernel<1><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const int BN = gemm_bn_for(M);
+  CUtensorMap tx, tw;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(gemm::BK), static_cast<cuuint32_t>(BN)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      *why = "cuTensorMapEncodeTiled failed for the activation tensor";
+      return cudaErrorInvalidValue;
+    }
+  }
+  {
+    const int64_t row_bytes = (fmt == 2) ? K / 2 : K;
+    const cuuint32_t raw_row = (fmt == 2) ? GemmCfg<2>::RAW_ROW : GemmCfg<1>::RAW_ROW;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    cuuint32_t box[2] = {raw_row, static_cast<cuuint32_t>(gemm::BM)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(codes), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     fmt == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      *why = "cuTensorMapEncodeTiled failed for the weight codes";
+      return cudaErrorInvalidValue;
+    }
+  }
+  GemmParams p;
+  p.s16 = reinterpret_cast<const __half*>(scales);
+  p.bias = reinterpret_cast<const uint16_t*>(bias);
+  p.y = reinterpret_cast<uint16_t*>(y);
+  p.tokscale = tokscale;
+  p.M = M; p.N = N; p.K = K; p.ldy = ldy;
+  p.acc = acc;
+  p.m_blocks = static_cast<int>((N + gemm::BM - 1) / gemm::BM);
+  p.n_blocks = static_cast<int>((M + BN - 1) / BN);
+  p.tiles = p.m_blocks * p.n_blocks;
+  p.ksteps = static_cast<int>(K / gemm::BK);
+  if (fmt == 2) {
+    if (BN == 64) return launch_gemm_t<2, 64>(tx, tw, p, sms, st);
+    if (BN == 128) return launch_gemm_t<2, 128>(tx, tw, p, sms, st);
+    return launch_gemm_t<2, 256>(tx, tw, p, sms, st);
+  }
+  if (BN == 64) return launch_gemm_t<1, 64>(tx, tw, p, sms, st);
+  if (BN == 128) return launch_gemm_t<1, 128>(tx, tw, p, sms, st);
+  return launch_gemm_t<1, 256>(tx, tw, p, sms, st);
+}
+
+}  // namespace lb

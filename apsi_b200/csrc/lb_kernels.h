@@ -1,0 +1,29 @@
+// Internal launchers (host side) shared between the kernel files and the C ABI in lb_api.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace lb {
+
+cudaError_t launch_quant_int4_g128(const void* w, int dt, int64_t N, int64_t K, uint8_t* packed, uint16_t* s16,
+                                   float* s32, int sms, cudaStream_t st);
+cudaError_t launch_quant_int8_rows(const void* w, int dt, int64_t N, int64_t K, int8_t* codes, uint16_t* s16,
+                                   float* s32, int sms, cudaStream_t st);
+cudaError_t launch_quant_g32(int kind, const void* w, int dt, int64_t N, int64_t K, uint32_t* words, float* s32,
+                             int sms, cudaStream_t st);
+cudaError_t launch_dequant(int fmt, const void* codes, const void* scales, int sf32, int64_t N, int64_t K,
+                           void* out, int out_dt, int sms, cudaStream_t st);
+
+int gemv_max_k(int fmt);
+cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
+                        int64_t N, const void* bias, int acc, void* y, int64_t ldy, cudaStream_t st);
+
+size_t gemm_workspace_bytes(int64_t M, int64_t K);
+cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
+                        int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
+                        cudaStream_t st, const char** why);
+
+cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, cudaStream_t st);
+
+}  // namespace lb

@@ -1,0 +1,5 @@
+// The whole library as one translation unit (one definition of the device error word, no device linking).
+#include "lb_quant.cu"
+#include "lb_gemv.cu"
+#include "lb_gemm.cu"
+#include "lb_api.cu"

@@ -1,0 +1,190 @@
+"""Torch-level wrappers of the C ABI: device tensors in, device tensors out, on the current CUDA stream.
+
+Torch supplies device memory and streams only; every computation is one of the library's sm_100a kernels.
+Inputs that are not CUDA tensors are rejected (there is no CPU path here).
+"""
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F32, DT_BF16, LowbitError
+
+__all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "dequant", "linear",
+           "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
+           "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError"]
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need_cuda(t, name):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise LowbitError(_lib.LB_E_DEVICE, f"{name} must be a CUDA tensor (the B200 path has no CPU fallback)")
+    if not t.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, f"{name} must be contiguous")
+
+
+def _weight_dtype(w):
+    if w.dtype == torch.float32:
+        return DT_F32
+    if w.dtype == torch.bfloat16:
+        return DT_BF16
+    raise LowbitError(_lib.LB_E_ARG, f"weights must be float32 or bfloat16, got {w.dtype}")
+
+
+# ------------------------------------------------------------------------------------------------ quantise
+def quant_int8_rows(w, want_scale32=True):
+    """int8 codes [N, K], fp16 scales [N] (and the reference's fp32 scales [N]) of a [N, K] weight."""
+    _need_cuda(w, "w")
+    N, K = w.shape
+    codes = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    s16 = torch.empty((N,), dtype=torch.float16, device=w.device)
+    s32 = torch.empty((N,), dtype=torch.float32, device=w.device) if want_scale32 else None
+    with torch.cuda.device(w.device):
+        _lib.call("lb_quant_int8_rows", _ptr(w), _weight_dtype(w), N, K, _ptr(codes), _ptr(s16), _ptr(s32),
+                  _stream(w.device))
+    return codes, s16, s32
+
+
+def quant_int4_g128(w, want_scale32=True):
+    """Packed int4 [N, K/2] (uint8), fp16 scales [N, K/128] (and fp32 scales) of a [N, K] weight."""
+    _need_cuda(w, "w")
+    N, K = w.shape
+    packed = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    s16 = torch.empty((N, K // 128), dtype=torch.float16, device=w.device)
+    s32 = torch.empty((N, K // 128), dtype=torch.float32, device=w.device) if want_scale32 else None
+    with torch.cuda.device(w.device):
+        _lib.call("lb_quant_int4_g128", _ptr(w), _weight_dtype(w), N, K, _ptr(packed), _ptr(s16), _ptr(s32),
+                  _stream(w.device))
+    return packed, s16, s32
+
+
+def quant_q8_0_g32(w):
+    """hub_gpu-layout int8 words [N, K/4] (int32 storage of uint32 words) and fp32 scales [N, K/32]."""
+    _need_cuda(w, "w")
+    N, K = w.shape
+    words = torch.empty((N, K // 4), dtype=torch.int32, device=w.device)
+    s32 = torch.empty((N, K // 32), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        _lib.call("lb_quant_q8_0_g32", _ptr(w), _weight_dtype(w), N, K, _ptr(words), _ptr(s32), _stream(w.device))
+    return words, s32
+
+
+def quant_q4_0_g32(w):
+    """hub_gpu-layout int4 words [N, K/8] (nibble = q + 8) and fp32 scales [N, K/32]."""
+    _need_cuda(w, "w")
+    N, K = w.shape
+    words = torch.empty((N, K // 8), dtype=torch.int32, device=w.device)
+    s32 = torch.empty((N, K // 32), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        _lib.call("lb_quant_q4_0_g32", _ptr(w), _weight_dtype(w), N, K, _ptr(words), _ptr(s32), _stream(w.device))
+    return words, s32
+
+
+# ------------------------------------------------------------------------------------------------ dequantise
+def dequant(fmt, codes, scales, N, K, out_dtype=torch.float32, scale_f32=None):
+    """code * scale as [N, K] float32 (or bfloat16).  The scale dtype follows the tensor (float16 or float32)."""
+    _need_cuda(codes, "codes")
+    _need_cuda(scales, "scales")
+    out = torch.empty((N, K), dtype=out_dtype, device=codes.device)
+    dt = DT_F32 if out_dtype == torch.float32 else DT_BF16
+    sdt = DT_F32 if scales.dtype == torch.float32 else _lib.DT_F16
+    with torch.cuda.device(codes.device):
+        _lib.call("lb_dequant", fmt, _ptr(codes), _ptr(scales), sdt, N, K, _ptr(out), dt, _stream(codes.device))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ products
+_ws_lock = threading.Lock()
+_ws = {}
+
+
+def linear_workspace_bytes(fmt, M, N, K):
+    n = ctypes.c_size_t(0)
+    _lib.call("lb_linear_workspace_size", fmt, M, N, K, ctypes.byref(n))
+    return n.value
+
+
+def _workspace(device, nbytes):
+    """A per-device scratch buffer of at least nbytes (grown on demand, never shrunk)."""
+    if nbytes == 0:
+        return None
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+_fast = {}
+
+
+def _fn(name):
+    f = _fast.get(name)
+    if f is None:
+        f = _fast[name] = getattr(_lib.load(), name)
+    return f
+
+
+def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False):
+    """y[M, N] = x[M, K] . deq(W)^T (+ bias) (+ out if accumulate), bf16 out, fp32 accumulation.
+
+    This is the per-call hot path of the host layer, so it avoids anything but pointer and size lookups."""
+    if not (isinstance(x, torch.Tensor) and x.is_cuda):
+        _need_cuda(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise LowbitError(_lib.LB_E_ARG, f"x must be bfloat16, got {x.dtype}")
+    K = x.shape[-1]
+    M = x.numel() // K
+    if not x.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "x must be contiguous")
+    dev = x.device
+    if out is None:
+        if accumulate:
+            raise LowbitError(_lib.LB_E_ARG, "accumulate needs an output tensor")
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ldy = out.stride(-2) if out.dim() >= 2 else N
+    switch = dev.index != torch.cuda.current_device()
+    if switch:
+        prev = torch.cuda.current_device()
+        torch.cuda.set_device(dev)
+    try:
+        nbytes = 0 if M <= 16 else linear_workspace_bytes(fmt, M, N, K)
+        ws = _workspace(dev, nbytes) if nbytes else None
+        rc = _fn("lb_linear")(fmt, x.data_ptr(), M, K, codes.data_ptr(), scales.data_ptr(), N,
+                              bias.data_ptr() if bias is not None else None, 1 if accumulate else 0,
+                              out.data_ptr(), ldy, ws.data_ptr() if ws is not None else None, nbytes,
+                              torch.cuda.current_stream(dev).cuda_stream)
+    finally:
+        if switch:
+            torch.cuda.set_device(prev)
+    if rc:
+        _lib.check(rc)
+    return out
+
+
+def interleave_cols(src, G, M, Nl):
+    """[G][M][Nl] rank-major shards -> [M][G*Nl]."""
+    _need_cuda(src, "src")
+    dst = torch.empty((M, G * Nl), dtype=src.dtype, device=src.device)
+    with torch.cuda.device(src.device):
+        _lib.call("lb_interleave_cols", _ptr(src), G, M, Nl, _ptr(dst), _stream(src.device))
+    return dst
+
+
+def device_errors(device=None):
+    """Reads and clears the device error word (bit 1: a bounded in-kernel wait gave up)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    v = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        _lib.call("lb_device_errors", _stream(device), ctypes.byref(v))
+    return v.value

@@ -1,0 +1,316 @@
+"""The public entry points of ``apsi/precision.py`` on the B200 library.
+
+Same names, argument meanings and error types as the reference module (apsi/precision.py:142-339) for the
+formats on the B200 path:
+
+* ``quantize(x, "int8", axis=0)`` -- int8 with one absmax/127 scale per row of a 2-D array (bit-exact with the
+  reference: codes, float32 scale); the QTensor also carries the binary16 scale the kernels use.
+* ``quantize(x, "int4", axis=0, group=128)`` -- int4 with one absmax/7 scale per 128 values along each row;
+  bit-exact with ``quantize(x.reshape(-1, 128), "int4", axis=0)`` of the reference.  ``group`` is the one new
+  keyword.  A 2-D ``[R, 128]`` array with ``axis=0`` (the reference's own spelling) takes the same kernel.
+* ``dequantize(q)``, ``qmatmul(a, b)``, ``round_to``, ``quant_error``, ``nbytes``, ``QTensor``, ``FORMATS``.
+* ``quantize_linear(W, fmt)`` -- new: quantizes an Apsi ``Linear`` weight stored ``[in, out]`` into the kernel
+  layout (rows = outputs, groups along the inputs); ``qmatmul(x, q)`` / ``x @ q`` then run the fused
+  dequantise-and-matmul kernels.
+
+Every computation runs on the GPU.  NumPy inputs are copied to the current CUDA device, processed there and
+the results copied back; torch CUDA inputs stay on the device.  Formats, axes or scale modes the B200 path does
+not implement raise ``RuntimeErr`` with the reason (the reference's error type), never a silent CPU path.
+"""
+import math
+
+import numpy as np
+
+from . import kernels as _k
+from ._lib import FMT_INT8_ROW, FMT_INT4_G128, LowbitError
+
+__all__ = ["RuntimeErr", "Format", "FORMATS", "ALIASES", "get_format", "QTensor", "quantize", "dequantize",
+           "round_to", "qmatmul", "nbytes", "quant_error", "format_info", "quantize_linear", "module"]
+
+
+class RuntimeErr(Exception):
+    """Error type of the reference language runtime (apsi/errors.py RuntimeErr) for bad precision requests."""
+
+
+class Format:
+    """A numeric format.  The B200 path implements the integer formats; the table keeps the reference's
+    names so ``get_format`` accepts the same spellings (apsi/precision.py:43-74)."""
+
+    def __init__(self, name, bits, kind, qmax=None):
+        self.name, self.bits, self.kind = name, bits, kind
+        self.qmax = qmax
+        self.max = float(qmax) if qmax is not None else None
+
+    def __repr__(self):
+        return self.name
+
+
+FORMATS = {
+    "int8": Format("int8", 8, "int", qmax=127),
+    "int4": Format("int4", 4, "int", qmax=7),
+}
+# names the reference knows whose quantisation is not on the B200 path (error message, not silence)
+_OTHER = ("f64", "f32", "f16", "bf16", "fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1", "uint8")
+ALIASES = {"fp64": "f64", "fp32": "f32", "fp16": "f16", "fp8": "fp8_e4m3", "bf8": "fp8_e5m2",
+           "e4m3": "fp8_e4m3", "e5m2": "fp8_e5m2", "fp6": "fp6_e3m2", "fp4": "fp4_e2m1",
+           "int4_g128": "int4", "w4g128": "int4", "w8": "int8"}
+
+
+def get_format(f):
+    name = getattr(f, "name", f)
+    name = ALIASES.get(name, name)
+    if name in FORMATS:
+        return FORMATS[name]
+    if name in _OTHER:
+        raise RuntimeErr(f"numeric format '{name}' is not on the B200 low-bit path (int8, int4)")
+    raise RuntimeErr(f"unknown numeric format '{name}'; choose one of {', '.join(FORMATS)}")
+
+
+# ------------------------------------------------------------------------------------------------ QTensor
+class QTensor:
+    """Codes + scales of a quantised array (apsi/precision.py:142-165), with the kernel layout attached.
+
+    ``codes``/``scale`` follow the reference (flat uint8 codes -- int4 packed two per byte, low nibble first --
+    and float32 scales shaped as the reference returns them).  B200 additions: ``scale16`` (the binary16
+    scales the kernels read), ``group`` (128 for int4 groups, None for one scale per row), ``kn`` (True when
+    the logical array is ``[in, out]`` and the rows stored are its transpose, see ``quantize_linear``)."""
+    __slots__ = ("codes", "scale", "fmt", "shape", "axis", "dim", "packed", "scale16", "group", "kn", "_dev")
+
+    def __init__(self, codes, scale, fmt, shape, axis, dim=None, packed=False, scale16=None, group=None, kn=False):
+        self.codes, self.scale, self.fmt, self.shape = codes, scale, fmt, tuple(shape)
+        self.axis, self.dim, self.packed = axis, dim, packed
+        self.scale16, self.group, self.kn = scale16, group, kn
+        self._dev = None
+
+    @property
+    def nbytes(self):
+        n = _nbytes_of(self.codes)
+        if self.scale16 is not None:
+            n += _nbytes_of(self.scale16)
+        elif self.scale is not None and not isinstance(self.scale, float):
+            n += _nbytes_of(self.scale)
+        return n
+
+    @property
+    def ndim(self):
+        return len(self.shape)
+
+    @property
+    def rows(self):
+        """(rows, cols) of the stored row-major code matrix (outputs x inputs for a linear weight)."""
+        return (self.shape[1], self.shape[0]) if self.kn else (self.shape[0], int(np.prod(self.shape[1:])))
+
+    @property
+    def kernel_format(self):
+        return FMT_INT4_G128 if self.fmt.bits == 4 else FMT_INT8_ROW
+
+    def device_tensors(self, device=None):
+        """(codes, scale16) as CUDA tensors in the kernel layout (cached for host QTensors)."""
+        import torch
+        if _is_torch(self.codes) and self.codes.is_cuda:
+            return self.codes, self.scale16
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self._dev is None or self._dev[0] != dev:
+            R, C = self.rows
+            ncols = C // 2 if self.fmt.bits == 4 else C
+            codes = torch.from_numpy(np.ascontiguousarray(self.codes).view(np.uint8).reshape(R, ncols)).to(dev)
+            s16 = torch.from_numpy(np.ascontiguousarray(self.scale16)).to(dev)
+            self._dev = (dev, codes, s16)
+        return self._dev[1], self._dev[2]
+
+    def dequantize(self):
+        return dequantize(self)
+
+    def __matmul__(self, other):
+        raise RuntimeErr("a quantised weight is the right operand: write x @ q")
+
+    def __rmatmul__(self, x):
+        return qmatmul(x, self)
+
+    def __repr__(self):
+        g = f", g{self.group}" if self.group else ""
+        return f"QTensor[{'x'.join(map(str, self.shape))}, {self.fmt.name}{g}, {self.nbytes} bytes]"
+
+
+def _is_torch(a):
+    try:
+        import torch
+        return isinstance(a, torch.Tensor)
+    except ImportError:  # pragma: no cover
+        return False
+
+
+def _nbytes_of(a):
+    if _is_torch(a):
+        return a.numel() * a.element_size()
+    return int(np.asarray(a).nbytes)
+
+
+def _to_device_weight(x):
+    """(torch CUDA tensor float32/bfloat16 [R, C], was_numpy)."""
+    import torch
+    if _is_torch(x):
+        if not x.is_cuda:
+            x = x.cuda()
+        if x.dtype not in (torch.float32, torch.bfloat16):
+            x = x.float()
+        return x.contiguous(), False
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    return torch.from_numpy(a).cuda(), True
+
+
+# ------------------------------------------------------------------------------------------------ quantise
+def quantize(x, fmt, scale="auto", axis=None, group=None):
+    """Quantise an array on the GPU (apsi/precision.py:216-246 semantics for int8 / int4).
+
+    Supported: 2-D arrays with ``axis=0`` (one scale per row), and for int4 ``group=128`` (one scale per 128
+    values along each row).  ``scale`` must be "auto"."""
+    f = get_format(fmt)
+    if scale != "auto":
+        raise RuntimeErr("the B200 path quantises with scale='auto' (absmax) only")
+    if getattr(x, "ndim", np.ndim(x)) != 2 or axis not in (0, -2):
+        raise RuntimeErr("the B200 path quantises 2-D arrays with axis=0 (one scale per row, or per row group)")
+    R, C = (int(s) for s in x.shape)
+    if f.bits == 4:
+        if group is None and C == 128:
+            group = 128                                   # quantize(W.reshape(-1, 128), "int4", axis=0)
+        if group != 128:
+            raise RuntimeErr("int4 on the B200 path uses groups of 128 along the row (group=128)")
+        if C % 128:
+            raise RuntimeErr(f"int4 groups of 128 need a row length that is a multiple of 128 (got {C})")
+    else:
+        if group not in (None, C):
+            raise RuntimeErr("int8 on the B200 path uses one scale per row (group=None)")
+        if C % 8:
+            raise RuntimeErr(f"int8 rows need a length that is a multiple of 8 (got {C})")
+        group = None
+    w, was_np = _to_device_weight(x)
+    if f.bits == 4:
+        codes, s16, s32 = _k.quant_int4_g128(w)
+        scale_shape = (R * C // 128, 1) if group == 128 and C == 128 else (R, C // 128)
+    else:
+        codes, s16, s32 = _k.quant_int8_rows(w)
+        scale_shape = (R, 1)
+    if was_np:
+        codes = codes.cpu().numpy().reshape(-1).view(np.uint8)
+        s32 = s32.cpu().numpy().reshape(scale_shape)
+        s16 = s16.cpu().numpy()
+    else:
+        s32 = s32.reshape(scale_shape)
+    return QTensor(codes, s32, f, (R, C), axis, None, f.bits == 4, scale16=s16, group=group)
+
+
+def quantize_linear(W, fmt="int4", group=128):
+    """An Apsi Linear weight ``W[in, out]`` quantised for the fused kernels: rows are the outputs, the scales run
+    along the inputs (int8: one per output; int4: one per 128 inputs).  ``x @ q`` computes ``x @ W``.
+
+    The rounding is the reference's own quantize applied to ``W.T`` (per output row / group)."""
+    import torch
+    f = get_format(fmt)
+    if _is_torch(W):
+        Wt = W.detach().t().contiguous()
+    else:
+        Wt = np.ascontiguousarray(np.asarray(W, np.float32).T)
+    q = quantize(Wt, f, axis=0, group=group if f.bits == 4 else None)
+    q.shape = (q.shape[1], q.shape[0])
+    q.kn = True
+    del torch
+    return q
+
+
+# ------------------------------------------------------------------------------------------------ dequantise
+def dequantize(q):
+    """float32 values ``code * scale`` (apsi/precision.py:249-274), computed on the GPU with the float32 scale
+    (bit-exact with the reference).  Returns NumPy for host QTensors, a CUDA tensor for device ones."""
+    if not isinstance(q, QTensor):
+        return q
+    import torch
+    R, C = q.rows
+    fmt = q.kernel_format
+    on_host = not _is_torch(q.codes)
+    codes, _ = q.device_tensors()
+    s32 = q.scale
+    s32 = torch.from_numpy(np.ascontiguousarray(s32, np.float32)).to(codes.device) if on_host else s32
+    out = _k.dequant(fmt, codes, s32.reshape(-1), R, C, out_dtype=torch.float32, scale_f32=True)
+    if q.kn:
+        out = out.t().contiguous()
+    if on_host:
+        return out.cpu().numpy().reshape(q.shape)
+    return out.reshape(q.shape)
+
+
+# ------------------------------------------------------------------------------------------------ products
+def qmatmul(a, b, out=None):
+    """``a @ b`` with a quantised right operand on the fused kernels (apsi/precision.py:294-299).
+
+    ``b`` must be a QTensor in the kernel layout (``quantize_linear``, or ``quantize(W, ..., axis=0)`` of a
+    ``[N, K]`` weight, which multiplies as ``a @ W.T`` -- the hub / HF orientation).  ``a`` is ``[..., K]``:
+    a CUDA tensor stays on the device (bfloat16 out); NumPy / CPU inputs are copied in and the result copied
+    back as float32 (NumPy) or bfloat16 (torch).  ``out`` (B200 extension): a bfloat16 CUDA tensor ``[..., N]``
+    to write into (CUDA inputs only)."""
+    import torch
+    if isinstance(a, QTensor):
+        raise RuntimeErr("the B200 path quantises the weight (right) operand only")
+    if not isinstance(b, QTensor):
+        raise RuntimeErr("qmatmul on the B200 path needs a quantised right operand")
+    R, C = b.rows
+    was_np = not _is_torch(a)
+    if was_np:
+        xa = np.asarray(a)
+        xt = torch.from_numpy(np.ascontiguousarray(xa, np.float32))
+    else:
+        xt = a
+    lead = tuple(xt.shape[:-1])
+    if xt.shape[-1] != C:
+        raise RuntimeErr(f"shapes {tuple(xt.shape)} and {b.shape} do not multiply")
+    host = not xt.is_cuda
+    dev = torch.device("cuda", torch.cuda.current_device()) if host else xt.device
+    x2 = xt.reshape(-1, C)
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    x2 = x2.to(dev, non_blocking=True).contiguous()
+    codes, s16 = b.device_tensors(dev)
+    if out is not None and not host:
+        _k.linear(b.kernel_format, x2, codes, s16, R, out=out.view(-1, R))
+        return out
+    y = _k.linear(b.kernel_format, x2, codes, s16, R)
+    y = y.reshape(*lead, R)
+    if host:
+        y = y.to("cpu")
+    if was_np:
+        return y.float().numpy()
+    return y
+
+
+def round_to(x, fmt, scale="auto", axis=None, group=None):
+    """What the format stores, as an ordinary float array (apsi/precision.py:278-292, no autodiff here)."""
+    r = dequantize(quantize(x, fmt, scale, axis, group))
+    return np.asarray(r, dtype=np.float64) if not _is_torch(r) else r
+
+
+def nbytes(x):
+    if isinstance(x, QTensor):
+        return x.nbytes
+    return _nbytes_of(x)
+
+
+def quant_error(x, fmt, axis=0, group=None):
+    """Relative RMS error of storing x in `fmt` (apsi/precision.py:310-316)."""
+    xv = np.asarray(x, dtype=np.float64)
+    r = np.asarray(round_to(np.asarray(x, np.float32), fmt, "auto", axis, group), dtype=np.float64)
+    denom = math.sqrt(float(np.mean(xv * xv))) or 1.0
+    return math.sqrt(float(np.mean((r - xv) ** 2))) / denom
+
+
+def format_info(fmt):
+    f = get_format(fmt)
+    return {"name": f.name, "bits": f.bits, "max": f.max, "eps": 1.0, "tiny": 1.0}
+
+
+def module():
+    return {"quantize": quantize, "dequantize": dequantize, "round_to": round_to, "qmatmul": qmatmul,
+            "nbytes": nbytes, "quant_error": quant_error, "format_info": format_info,
+            "quantize_linear": quantize_linear}
+
+
+__all__ += ["LowbitError"]

@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 low-bit linear layer (the contract of this repository's bench).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Metric: int4-g128 weight-only GEMV weight GB/s at M=1, on configs[1] (x bf16 [1, 4096],
+W [11008, 4096] ~ N(0, 0.02) quantised to int4 with fp16 absmax/7 scales per 128 values).
+
+A step is one decode token through LAYERS = 128 resident, distinct int4-g128 weight matrices of that shape
+(2.98 GB of packed weights -- the weight bytes of one decode step of the 7B-class decoder in configs[3]), so
+every GEMV streams its weights from HBM (inputs are larger than L2; nothing is flushed).  The step is one
+CUDA-graph replay of 128 GEMV launches.  ``value`` is packed weight bytes per second over all ranks.
+
+N > 1 (torchrun): each rank holds the column shards of 128 layers that are N times as wide (weak scaling:
+[11008, 4096] per rank per layer); after the GEMVs the N-sharded outputs are reassembled with an NCCL
+all-gather plus one interleave kernel, inside the timed region; the all-gather is also timed on its own.
+
+Also reported: the GEMV's live roofline (CUDA events on the launching stream), ``e2e`` through the public API
+(``apsi_b200.precision.qmatmul``) from pinned host memory and back, the reference CPU path (the oracle port of
+``precision.qmatmul``) as ``cpu_baseline``, and the prefill GEMM of configs[2] (M=2048, N=12288, K=4096).
+"""
+import argparse
+import json
+import os
+import re
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "int4-g128 W-only GEMV weight GB/s (M=1) & GEMM TFLOP/s (M=2048) vs roofline, 1–8 GPU"
+M1, N1, K1 = 1, 11008, 4096          # configs[1]
+LAYERS = 128
+GM, GN, GK = 2048, 12288, 4096       # configs[2]
+FALLBACK_HBM, FALLBACK_TF = 6650.0, 1590.0
+
+
+def gemv_bytes(M, N, K):
+    """Algorithmic bytes of one int4-g128 GEMV: packed codes + fp16 scales + x + y."""
+    return N * K // 2 + N * (K // 128) * 2 + M * K * 2 + M * N * 2
+
+
+def weight_bytes(N, K):
+    return N * K // 2 + N * (K // 128) * 2
+
+
+def read_peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM, FALLBACK_TF, "fallback"
+
+
+def read_traffic(name):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded by an ncu capture in
+    profiles/<name>.md as a line 'traffic_bytes_per_launch: N' (None when absent)."""
+    try:
+        with open(os.path.join(HERE, "profiles", name + ".md")) as fh:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", fh.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every `period` seconds in a thread."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, index, period=0.002):
+        self.samples = []
+        self.period = period
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:                      # noqa: BLE001 - no NVML: report no clocks
+            self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def _sample(self):
+        nv = self.nv
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+            try:
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:                  # noqa: BLE001
+                rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+            self.samples.append((time.perf_counter(), sm, rs))
+        except Exception:                      # noqa: BLE001
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not win:                            # region shorter than the period: nearest samples
+            win = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        mhz = [s[1] for s in win]
+        bits = 0
+        for s in win:
+            bits |= s[2]
+        reasons = [n for b, n in self.REASONS.items() if bits & b]
+        return {"sm_mhz": float(np.median(mhz)) if mhz else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(win)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline_sample(reps=2):
+    """The reference's CPU path for an int4 product (precision.qmatmul = dequantise + float32 matmul,
+    restated in oracle/), on [11008, 4096] weights at M=1: packed-weight GB/s."""
+    import oracle as O
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((N1, K1)) * 0.02).astype(np.float32)
+    packed, _, s16 = O.quant_int4_g128(W)
+    x = O.bf16_round(rng.standard_normal((M1, K1)).astype(np.float32))
+    O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")        # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
+    dt = (time.perf_counter() - t0) / reps
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:                          # noqa: BLE001
+        cores = os.cpu_count()
+    return weight_bytes(N1, K1) / dt / 1e9, dt, cores
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    import oracle as O
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((N1, K1)) * 0.02).astype(np.float32)
+    packed, _, s16 = O.quant_int4_g128(W)
+    x = O.bf16_round(rng.standard_normal((M1, K1)).astype(np.float32))
+    for _ in range(args.warmup):
+        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
+    dt = (time.perf_counter() - t0) / args.steps
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:                          # noqa: BLE001
+        cores = os.cpu_count()
+    val = weight_bytes(N1, K1) / dt / 1e9
+    sample = "one [11008,4096] int4-g128 product per step (M=1): dequantise (NumPy) + float32 matmul (BLAS)"
+    out = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "configs[1]: int4-g128 GEMV M=1, W[11008,4096] (bounded sample: 1 layer per step)",
+                      "M": M1, "N": N1, "K": K1, "path": "oracle port of precision.qmatmul (CPU)"},
+           "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from apsi_b200 import kernels as Kn
+    from apsi_b200 import precision as P
+    from apsi_b200._lib import FMT_INT4_G128
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    hbm_peak, tf_peak, peak_kind = read_peaks()
+
+    # ---- resident inputs: LAYERS distinct weight shards, quantised on the device (not timed)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    packed, scales = [], []
+    for _ in range(LAYERS):
+        W = torch.randn((N1, K1), generator=gen, device=dev) * 0.02
+        p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+        packed.append(p)
+        scales.append(s16)
+        del W
+    x = torch.randn((M1, K1), generator=gen, device=dev).to(torch.bfloat16)
+    ys = torch.empty((LAYERS, M1, N1), dtype=torch.bfloat16, device=dev)
+    gathered = torch.empty((world, LAYERS * M1, N1), dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    def sweep():
+        for i in range(LAYERS):
+            Kn.linear(FMT_INT4_G128, x, packed[i], scales[i], N1, out=ys[i])
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        sweep()                                            # first use (device init, lazy setup) outside capture
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        sweep()
+    torch.cuda.synchronize(dev)
+
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+
+    def step(i=None):
+        with torch.cuda.stream(stream):
+            if i is not None:
+                ev_a[i].record(stream)
+            graph.replay()
+            if i is not None:
+                ev_b[i].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
+                Kn.interleave_cols(gathered, world, LAYERS * M1, N1)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clk = ClockSampler(local_rank)
+    clk.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    w1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    clk.stop()
+    elapsed = t_start.elapsed_time(t_end)                  # ms
+    gemv_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b))
+    tt = torch.tensor([elapsed, gemv_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    elapsed, gemv_ms = float(tt[0]), float(tt[1])
+    errs = Kn.device_errors(dev)
+
+    wb_step = LAYERS * weight_bytes(N1, K1) * world
+    value = wb_step * args.steps / (elapsed * 1e-3) / 1e9
+    launch_s = gemv_ms * 1e-3 / (args.steps * LAYERS)
+    achieved = gemv_bytes(M1, N1, K1) / launch_s / 1e9
+    traffic = read_traffic("gemv_int4_m1_11008x4096")
+
+    out = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 5), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int4xbf16->f32", "data": "synthetic",
+           "config": {"workload": "configs[1]: int4-g128 decode GEMV, M=1, W[11008,4096] per rank, "
+                                  f"{LAYERS} distinct resident weight matrices per step",
+                      "M": M1, "N": N1 * world, "N_per_rank": N1, "K": K1, "layers_per_step": LAYERS,
+                      "weight_bytes_per_step": wb_step, "l2": "inputs larger than L2 (no flush)",
+                      "parallelism": f"column-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                      "graph": "one CUDA graph replay of the GEMV launches per step"},
+           "roofline": {"kernel": "gemv_kernel<int4,1>", "bound": "hbm", "achieved": round(achieved, 1),
+                        "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                        "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs",
+                        "algorithmic_bytes_per_launch": gemv_bytes(M1, N1, K1),
+                        "avg_launch_us": round(launch_s * 1e6, 3)},
+           "gpu_launches": args.steps * LAYERS + (args.steps if world > 1 else 0),
+           "device_error_bits": errs}
+    out["clocks"] = clk.summary(w0, w1)
+
+    # ---- all-gather alone (N > 1)
+    if world > 1:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(5, args.steps)
+        with torch.cuda.stream(stream):
+            a0.record(stream)
+            for _ in range(reps):
+                dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
+            a1.record(stream)
+        torch.cuda.synchronize(dev)
+        ag = torch.tensor([a0.elapsed_time(a1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(ag, op=dist.ReduceOp.MAX)
+        per_rank = ys.numel() * 2 * (world - 1)
+        out["allgather"] = {"ms": round(float(ag), 4), "bytes_received_per_rank": per_rank,
+                            "GB_per_s_per_rank": round(per_rank / (float(ag) * 1e-3) / 1e9, 2)}
+
+    # ---- e2e through the public API: pinned host x in, every layer's y back to pinned host memory
+    qts = []
+    for i in range(LAYERS):
+        q = P.QTensor(packed[i], None, P.get_format("int4"), (N1, K1), 0, None, True, scale16=scales[i], group=128)
+        qts.append(q)
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((LAYERS, M1, N1), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        xd = x_host.to(dev, non_blocking=True)
+        for i in range(LAYERS):
+            P.qmatmul(xd, qts[i], out=ys[i])
+        y_host.copy_(ys, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    et = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_s = float(et)
+    out["e2e"] = {"value": round(wb_step / e2e_s / 1e9, 2), "unit": "GB/s",
+                  "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
+                  "api": "apsi_b200.precision.qmatmul per layer (one launch each, no graph)",
+                  "ms_per_step": round(e2e_s * 1e3, 3)}
+
+    # ---- prefill GEMM, configs[2] (rank 0 reports)
+    out["gemm"] = gemm_measure(torch, Kn, FMT_INT4_G128, dev, tf_peak, peak_kind)
+
+    if rank == 0 and world == 1:
+        try:
+            v, dt, cores = cpu_baseline_sample()
+            out["cpu_baseline"] = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                                   "sample": f"2 products of [11008,4096] int4-g128 at M=1 via the oracle port of "
+                                             f"precision.qmatmul ({dt * 1e3:.0f} ms each)"}
+        except Exception as e:               # noqa: BLE001
+            out["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
+                                   "sample": f"failed: {type(e).__name__}: {e}"}
+    del graph
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+def gemm_measure(torch, Kn, fmt, dev, tf_peak, peak_kind, reps=20):
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    W = torch.randn((GN, GK), generator=gen, device=dev) * 0.02
+    p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+    del W
+    x = torch.randn((GM, GK), generator=gen, device=dev)
+    hit = torch.rand((GM, GK), generator=gen, device=dev) < 0.001
+    x = torch.where(hit, x * 20, x).to(torch.bfloat16)
+    y = torch.empty((GM, GN), dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        Kn.linear(fmt, x, p, s16, GN, out=y)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        Kn.linear(fmt, x, p, s16, GN, out=y)
+    b.record()
+    torch.cuda.synchronize(dev)
+    s = a.elapsed_time(b) * 1e-3 / reps
+    flops = 2 * GM * GN * GK
+    tf = flops / s / 1e12
+    return {"workload": "configs[2]: int4-g128 GEMM M=2048 N=12288 K=4096, x with 0.1% outliers x20",
+            "us_per_call": round(s * 1e6, 2), "TFLOP_per_s": round(tf, 1),
+            "roofline": {"kernel": "gemm_kernel<int4,256> (+prep_x_kernel)", "bound": "tensor",
+                         "achieved": round(tf, 1), "peak": tf_peak, "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                         "peak_source": f"{peak_kind} bf16_tflops (burst)",
+                         "traffic": read_traffic("gemm_int4_m2048_12288x4096")}}
+
+
+def run_case(case):
+    """A short fixed workload for profiler captures (no JSON): a few launches of one kernel on one GPU.
+
+    gemv      int4-g128 GEMV, M=1, [11008, 4096], 8 rotating weight copies (186 MB > L2), 12 launches
+    gemv_down int4-g128 GEMV, M=1, [4096, 11008] (K split over a 2-CTA cluster), 12 launches
+    gemv_m16  int4-g128 GEMV, M=16, [11008, 4096], 12 launches
+    gemm      int4-g128 GEMM, M=2048, [12288, 4096], 4 launches (each also runs prep_x_kernel)
+    quant     int4-g128 quantisation of a float32 [11008, 4096] weight, 4 launches"""
+    import torch
+    from apsi_b200 import kernels as Kn
+    from apsi_b200._lib import FMT_INT4_G128
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    if case in ("gemv", "gemv_down", "gemv_m16"):
+        M, N, K = {"gemv": (1, 11008, 4096), "gemv_down": (1, 4096, 11008), "gemv_m16": (16, 11008, 4096)}[case]
+        ws = []
+        for _ in range(8):
+            W = torch.randn((N, K), generator=gen, device=dev) * 0.02
+            p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+            ws.append((p, s16))
+        x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        for i in range(12):
+            p, s16 = ws[i % 8]
+            Kn.linear(FMT_INT4_G128, x, p, s16, N, out=y)
+    elif case == "gemm":
+        W = torch.randn((GN, GK), generator=gen, device=dev) * 0.02
+        p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+        x = torch.randn((GM, GK), generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.empty((GM, GN), dtype=torch.bfloat16, device=dev)
+        for _ in range(4):
+            Kn.linear(FMT_INT4_G128, x, p, s16, GN, out=y)
+    elif case == "quant":
+        W = torch.randn((N1, K1), generator=gen, device=dev) * 0.02
+        for _ in range(4):
+            Kn.quant_int4_g128(W, want_scale32=True)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize(dev)
+    errs = Kn.device_errors(dev)
+    print(f"case {case} done, device error bits {errs}")
+    return 1 if errs else 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="profiling workload (see run_case); no JSON output")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.case:
+        return run_case(args.case)
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

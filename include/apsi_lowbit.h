@@ -1,0 +1,137 @@
+/*
+ * apsi_lowbit.h -- C ABI of the B200 (sm_100a) low-bit quantized linear layer.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, returns an int status (LB_OK == 0,
+ * negative LB_E_* on error; lb_last_error() gives the message of the calling thread's last failure) and is
+ * asynchronous on the given CUDA stream (`stream` is a cudaStream_t passed as void*, NULL = legacy default
+ * stream).  All tensor pointers are DEVICE pointers owned by the caller.  Shapes are row-major:
+ *
+ *   W      [N, K]     weights, N output features, K input features (the HF / hub_gpu layout)
+ *   x      [M, K]     bfloat16 activations, M tokens
+ *   y      [M, ldy]   bfloat16 outputs (ldy >= N)
+ *
+ * Formats (LB_FMT_*):
+ *   INT8_ROW   codes int8 [N, K]; scale16 IEEE binary16 [N]            (absmax/127 per output row)
+ *   INT4_G128  packed uint8 [N, K/2]; scale16 binary16 [N, K/128]      (absmax/7 per 128 values along K;
+ *              byte j of a row holds element 2j in the low nibble, element 2j+1 in the high nibble,
+ *              two's complement)
+ *   Q8_0_G32   words uint32 [N, K/4] (byte j of a word = value j); scale32 float [N, K/32]
+ *   Q4_0_G32   words uint32 [N, K/8] (nibble j of a word = value j + 8); scale32 float [N, K/32]
+ *
+ * Arguments are checked before anything is launched; a rejected call leaves the device untouched.
+ * There is no CPU fallback: without an sm_100 device every compute call fails with LB_E_DEVICE.
+ */
+#ifndef APSI_LOWBIT_H
+#define APSI_LOWBIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LB_VERSION 10000 /* 1.0.0 */
+
+/* status codes */
+#define LB_OK 0
+#define LB_E_ARG (-1)         /* null pointer, bad shape, bad format / dtype */
+#define LB_E_ALIGN (-2)       /* pointer or leading dimension not aligned as required */
+#define LB_E_DEVICE (-3)      /* no usable sm_100 device, or a CUDA runtime error during setup */
+#define LB_E_LAUNCH (-4)      /* a kernel launch failed */
+#define LB_E_WORKSPACE (-5)   /* workspace missing or smaller than lb_linear_workspace_size() */
+#define LB_E_UNSUPPORTED (-6) /* valid request this build does not implement */
+
+/* formats */
+#define LB_FMT_INT8_ROW 1
+#define LB_FMT_INT4_G128 2
+#define LB_FMT_Q8_0_G32 3
+#define LB_FMT_Q4_0_G32 4
+
+/* element types of weight inputs / dequantised outputs */
+#define LB_DT_F32 0
+#define LB_DT_BF16 1
+#define LB_DT_F16 2
+
+/* device error word bits (lb_device_errors) */
+#define LB_DEVERR_WAIT_TIMEOUT 1 /* a bounded device-side wait (mbarrier) gave up; the output is invalid */
+
+/* ---------------------------------------------------------------------------------------------- runtime */
+
+/* LB_VERSION of the loaded library.  Replaces nothing in the reference (library identity). */
+int lb_version(void);
+
+/* Message of the calling thread's most recent failed call ("" if none). */
+const char* lb_last_error(void);
+
+/* Checks that `device` is compute capability 10.x and caches its SM count and L2 size.
+ * Replaces hub_gpu.runner() device selection / Runner.__init__ kernel load (apsi/hub_gpu.py:1772-1796,
+ * 1366-1395).  Compute calls call it implicitly for the current device. */
+int lb_init(int device);
+
+/* Reads and clears the device error word of the current device (LB_DEVERR_* bits).  Synchronises
+ * `stream` first.  Replaces the CUresult check after launches (apsi/native/cuda.py:213-223). */
+int lb_device_errors(void* stream, int* bits_out);
+
+/* ---------------------------------------------------------------------------------------------- quantise */
+
+/* int8, one absmax/127 scale per output row.  w: [N, K] in `w_dtype` (LB_DT_F32 or LB_DT_BF16).
+ * codes: int8 [N, K]; scale16: binary16 [N]; scale32 (may be NULL): float [N] -- the reference's float32
+ * scale, bit-exact.  Codes are bit-exact with precision.quantize(W, "int8", axis=0).
+ * Replaces precision.quantize / _scale_for for fmt int8, axis 0 (apsi/precision.py:205-246). */
+int lb_quant_int8_rows(const void* w, int w_dtype, int64_t N, int64_t K, int8_t* codes, uint16_t* scale16,
+                       float* scale32, void* stream);
+
+/* int4, one absmax/7 scale per 128 values along K (K % 128 == 0).  packed: uint8 [N, K/2];
+ * scale16: binary16 [N, K/128]; scale32 (may be NULL): float [N, K/128].  Bit-exact with
+ * precision.quantize(W.reshape(-1, 128), "int4", axis=0) (apsi/precision.py:168-172, 205-246). */
+int lb_quant_int4_g128(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* packed, uint16_t* scale16,
+                       float* scale32, void* stream);
+
+/* ggml-style int8 / int4 with one float scale per 32 values along K (K % 32 == 0), in hub_gpu's device
+ * word layout.  Bit-exact with hub_gpu.qnumpy + the quant8 / quant4 kernels' packing
+ * (apsi/hub_gpu.py:1215-1241, 734-801; launched by Runner._quant, apsi/hub_gpu.py:1478-1481). */
+int lb_quant_q8_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t* words, float* scale32,
+                      void* stream);
+int lb_quant_q4_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t* words, float* scale32,
+                      void* stream);
+
+/* ---------------------------------------------------------------------------------------------- dequantise */
+
+/* out[N, K] = code * scale in `out_dtype` (LB_DT_F32: the exact float32 product, as precision.dequantize;
+ * LB_DT_BF16: that product rounded to nearest even).  `scales` are `scale_dtype`: LB_DT_F16 (the stored
+ * binary16 scales) or LB_DT_F32 (the reference's float32 scales, which makes the result bit-exact with
+ * precision.dequantize); the G32 formats take LB_DT_F32 only.  Replaces precision.dequantize
+ * (apsi/precision.py:249-274) and Runner._deq / the deq4, deq8 kernels (apsi/hub_gpu.py:918-950, 1483-1489). */
+int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, int64_t N, int64_t K, void* out,
+               int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- products */
+
+/* Bytes of device workspace lb_linear needs for this shape (0 when none).  Replaces the scratch buffers of
+ * _Base.ws (apsi/hub_gpu.py:1288-1295). */
+int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes);
+
+/* y[m, n] = sum_k x[m, k] * deq(W)[n, k] (+ bias[n]) (+ y[m, n] if accumulate), float32 accumulation,
+ * bfloat16 output.  x: bf16 [M, K] (row stride K, 16-byte aligned); bias: bf16 [N] or NULL; y: bf16 with row
+ * stride ldy.  M <= 16 runs the decode GEMV (integer codes exact in the tensor-core operands, scales applied
+ * per group in float32; needs no workspace); larger M runs the tcgen05 GEMM (fp16 operands, x rescaled per
+ * row by a power of two, float32 accumulation in tensor memory), whose converted activations live in
+ * `workspace` (lb_linear_workspace_size() bytes, 256-byte aligned, contents need no initialisation).
+ * Replaces precision.qmatmul / models.qlinear (apsi/precision.py:294-299, apsi/models.py:302-308) and
+ * _Base.linear -> Runner.gemv / Runner.gemm with bias and acc (apsi/hub_gpu.py:1305-1315, 1491-1528). */
+int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+              const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+              void* stream);
+
+/* ---------------------------------------------------------------------------------------------- multi-GPU */
+
+/* Reassembles column shards after an all-gather: src [G][M][Nl] (rank-major, bf16) -> dst [M][G*Nl].
+ * No reference counterpart (the reference has no multi-GPU inference, apsi/hub_gpu.py:1772-1796). */
+int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APSI_LOWBIT_H */
