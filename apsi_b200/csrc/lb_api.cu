@@ -239,7 +239,7 @@ int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, c
   if (r) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (use_gemv(M))
-    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, st), "gemv");
+    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, st), "gemv");
   const char* why = nullptr;
   cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why);
   if (e != cudaSuccess && why) return fail(LB_E_LAUNCH, "gemm: %s (%s)", why, cudaGetErrorString(e));

@@ -1,0 +1,80 @@
+"""The C ABI: the library loads, exports every entry point include/apsi_lowbit.h declares, and rejects bad
+arguments before touching a device (no compute call is made here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from apsi_b200 import _lib, build
+
+HEADER = os.path.join(build.ROOT, "include", "apsi_lowbit.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(lb_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    names = declared()
+    assert len(names) >= 12
+    bound = {n for n, _, _ in _lib.SIGNATURES}
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in bound, f"{n} has no ctypes signature"
+
+
+def test_version_matches_header(lib):
+    v = int(re.search(r"#define LB_VERSION (\d+)", open(HEADER).read()).group(1))
+    assert lib.lb_version() == v
+
+
+def test_constants_match_header():
+    text = open(HEADER).read()
+    for name, val in (("LB_E_ARG", _lib.LB_E_ARG), ("LB_E_UNSUPPORTED", _lib.LB_E_UNSUPPORTED),
+                      ("LB_FMT_INT4_G128", _lib.FMT_INT4_G128), ("LB_FMT_INT8_ROW", _lib.FMT_INT8_ROW),
+                      ("LB_DT_F16", _lib.DT_F16)):
+        m = re.search(rf"#define {name} \(?(-?\d+)\)?", text)
+        assert int(m.group(1)) == val, name
+
+
+def test_bad_arguments_are_rejected_before_launch(lib):
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(1 << 20)            # never dereferenced: the checks fail first
+    assert lib.lb_quant_int4_g128(null, 0, 4, 128, fake, fake, null, null) == _lib.LB_E_ARG
+    assert lib.lb_quant_int4_g128(fake, 0, 4, 100, fake, fake, null, null) == _lib.LB_E_ARG     # K % 128
+    assert b"multiple of 128" in lib.lb_last_error()
+    assert lib.lb_quant_int4_g128(fake, 7, 4, 128, fake, fake, null, null) == _lib.LB_E_ARG     # dtype
+    assert lib.lb_quant_int8_rows(fake, 0, 0, 64, fake, fake, null, null) == _lib.LB_E_ARG      # N = 0
+    assert lib.lb_linear(9, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_UNSUPPORTED
+    assert lib.lb_linear(2, fake, 1, 100, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ARG
+    assert lib.lb_linear(2, fake, 1, 128, fake, fake, 8, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ARG  # ldy
+    odd = ctypes.c_void_p((1 << 20) + 2)
+    assert lib.lb_linear(2, odd, 1, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ALIGN
+    assert lib.lb_dequant(2, fake, fake, 5, 4, 128, fake, 0, null) == _lib.LB_E_ARG             # scale dtype
+    assert lib.lb_dequant(3, fake, fake, _lib.DT_F16, 4, 128, fake, 0, null) == _lib.LB_E_ARG    # g32 needs f32
+
+
+def test_workspace_query(lib):
+    n = ctypes.c_size_t(123)
+    assert lib.lb_linear_workspace_size(2, 1, 4096, 4096, ctypes.byref(n)) == 0
+    assert n.value == 0                                         # the decode GEMV needs no workspace
+    assert lib.lb_linear_workspace_size(2, 2048, 4096, 4096, ctypes.byref(n)) == 0
+    assert n.value >= 2048 * 4096 * 2                           # fp16 activations of the GEMM
+    assert lib.lb_linear_workspace_size(4, 1, 4, 128, ctypes.byref(n)) == _lib.LB_E_UNSUPPORTED
+
+
+def test_python_layer_raises_loudly_without_a_device():
+    import torch
+    from apsi_b200 import kernels
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    with pytest.raises(_lib.LowbitError):
+        kernels.quant_int4_g128(torch.zeros(4, 128))
