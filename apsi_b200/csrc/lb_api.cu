@@ -211,20 +211,21 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
   return LB_OK;
 }
 
-int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
-              const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
-              void* stream) {
+int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+                 const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+                 unsigned flags, void* stream) {
   if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
+  if (flags & ~static_cast<unsigned>(LB_LINEAR_STATIC_WEIGHTS)) return fail(LB_E_ARG, "lb_linear: unknown flags");
   if (!x || !codes || !scales || !y) return fail(LB_E_ARG, "lb_linear: x, codes, scales and y are required");
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear: M, N, K must be positive");
   if (M > (1LL << 31) || N > (1LL << 31)) return fail(LB_E_ARG, "lb_linear: M and N must be below 2^31");
   const int64_t kmult = fmt == LB_FMT_INT4_G128 ? 128 : 64;
   if (K % kmult) return fail(LB_E_ARG, "lb_linear: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
   if (ldy < N) return fail(LB_E_ARG, "lb_linear: ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
-  if (!aligned(x, 16) || !aligned(codes, 16)) return fail(LB_E_ALIGN, "lb_linear: x and codes must be 16-byte aligned");
-  if (!aligned(y, 2) || !aligned(scales, 2) || (bias && !aligned(bias, 2)))
-    return fail(LB_E_ALIGN, "lb_linear: y, scales and bias must be 2-byte aligned");
+  if (!aligned(x, 16) || !aligned(codes, 16) || !aligned(scales, 16))
+    return fail(LB_E_ALIGN, "lb_linear: x, codes and scales must be 16-byte aligned");
+  if (!aligned(y, 2) || (bias && !aligned(bias, 2))) return fail(LB_E_ALIGN, "lb_linear: y and bias must be 2-byte aligned");
   if (use_gemv(M) && K > gemv_max_k(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: K (%lld) above %d is not supported for M <= 16", (long long)K,
                 gemv_max_k(fmt));
@@ -238,12 +239,19 @@ int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, c
   int r = current(&d);
   if (r) return r;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool pdl = (flags & LB_LINEAR_STATIC_WEIGHTS) != 0;
   if (use_gemv(M))
-    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, st), "gemv");
+    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, pdl, st), "gemv");
   const char* why = nullptr;
   cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why);
   if (e != cudaSuccess && why) return fail(LB_E_LAUNCH, "gemm: %s (%s)", why, cudaGetErrorString(e));
   return launched(e, "gemm");
+}
+
+int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+              const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+              void* stream) {
+  return lb_linear_ex(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, ws_bytes, 0u, stream);
 }
 
 int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst, void* stream) {

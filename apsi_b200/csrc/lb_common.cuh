@@ -16,8 +16,6 @@ namespace lb {
 // The library is compiled as one translation unit (lb_lib.cu), so this is its only definition.
 __device__ int g_dev_errors = 0;
 
-// Bounded waits: ~2^22 polls with nanosleep back-off above 64 polls is several seconds at most.
-constexpr uint32_t kWaitPolls = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -51,18 +49,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete.  Gives up after kWaitPolls polls (or at once when
-// *abort is set): records LB_DEVERR_WAIT_TIMEOUT, sets *abort so every other wait of the CTA returns at once,
-// and returns false.  Callers carry on (their output is invalid), so no CTA barrier is skipped.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+// try_wait that lets the hardware suspend the thread for up to `ns` nanoseconds while the phase is pending
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Programmatic dependent launch: let the next kernel on the stream start its independent prologue, and wait
+// for the previous kernel's results (both are no-ops when the launch did not opt in).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Waits for the phase with the given parity to complete.  Each try suspends for at most 1 ms; after
+// kWaitTries tries (a few seconds), or at once when *abort is set, it records LB_DEVERR_WAIT_TIMEOUT, sets
+// *abort so every other wait of the CTA returns at once, and returns false.  Callers carry on (their output is
+// invalid), so no CTA barrier is skipped.
+constexpr uint32_t kWaitTries = 4096;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < kWaitTries; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort) return false;
-    if (i > 64) __nanosleep(i > 4096 ? 1024 : 64);
   }
   *abort = 1;
   atomicOr(&g_dev_errors, 1);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;   // usual case: completes within one try
+  return mbar_wait_slow(bar, parity, abort);
 }
 
 // ------------------------------------------------------------------------------------------- TMA
@@ -215,6 +235,11 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {

@@ -17,7 +17,8 @@ cudaError_t launch_dequant(int fmt, const void* codes, const void* scales, int s
 
 int gemv_max_k(int fmt);
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
-                        int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, cudaStream_t st);
+                        int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
+                        cudaStream_t st);
 
 size_t gemm_workspace_bytes(int64_t M, int64_t K);
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,

@@ -135,9 +135,11 @@ def _fn(name):
     return f
 
 
-def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False):
+def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False, static_weights=False):
     """y[M, N] = x[M, K] . deq(W)^T (+ bias) (+ out if accumulate), bf16 out, fp32 accumulation.
 
+    ``static_weights``: no kernel still running on the current stream writes ``codes``/``scales`` (weights
+    quantised before the previous launch); the GEMV then overlaps its weight stream with that kernel.
     This is the per-call hot path of the host layer, so it avoids anything but pointer and size lookups."""
     if not (isinstance(x, torch.Tensor) and x.is_cuda):
         _need_cuda(x, "x")
@@ -160,10 +162,11 @@ def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False):
     try:
         nbytes = 0 if M <= 16 else linear_workspace_bytes(fmt, M, N, K)
         ws = _workspace(dev, nbytes) if nbytes else None
-        rc = _fn("lb_linear")(fmt, x.data_ptr(), M, K, codes.data_ptr(), scales.data_ptr(), N,
-                              bias.data_ptr() if bias is not None else None, 1 if accumulate else 0,
-                              out.data_ptr(), ldy, ws.data_ptr() if ws is not None else None, nbytes,
-                              torch.cuda.current_stream(dev).cuda_stream)
+        rc = _fn("lb_linear_ex")(fmt, x.data_ptr(), M, K, codes.data_ptr(), scales.data_ptr(), N,
+                                 bias.data_ptr() if bias is not None else None, 1 if accumulate else 0,
+                                 out.data_ptr(), ldy, ws.data_ptr() if ws is not None else None, nbytes,
+                                 _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0,
+                                 torch.cuda.current_stream(dev).cuda_stream)
     finally:
         if switch:
             torch.cuda.set_device(prev)

@@ -215,7 +215,7 @@ def run_ours(args, rank, world, local_rank):
 
     def sweep():
         for i in range(LAYERS):
-            Kn.linear(FMT_INT4_G128, x, packed[i], scales[i], N1, out=ys[i])
+            Kn.linear(FMT_INT4_G128, x, packed[i], scales[i], N1, out=ys[i], static_weights=True)
 
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))

@@ -53,6 +53,9 @@ extern "C" {
 #define LB_DT_BF16 1
 #define LB_DT_F16 2
 
+/* lb_linear_ex flags */
+#define LB_LINEAR_STATIC_WEIGHTS 1u /* no kernel still running on the stream writes codes or scales */
+
 /* device error word bits (lb_device_errors) */
 #define LB_DEVERR_WAIT_TIMEOUT 1 /* a bounded device-side wait (mbarrier) gave up; the output is invalid */
 
@@ -118,11 +121,21 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
  * per group in float32; needs no workspace); larger M runs the tcgen05 GEMM (fp16 operands, x rescaled per
  * row by a power of two, float32 accumulation in tensor memory), whose converted activations live in
  * `workspace` (lb_linear_workspace_size() bytes, 256-byte aligned, contents need no initialisation).
+ * x, codes and scales must be 16-byte aligned.
  * Replaces precision.qmatmul / models.qlinear (apsi/precision.py:294-299, apsi/models.py:302-308) and
  * _Base.linear -> Runner.gemv / Runner.gemm with bias and acc (apsi/hub_gpu.py:1305-1315, 1491-1528). */
 int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
               const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
               void* stream);
+
+/* lb_linear with flags.  LB_LINEAR_STATIC_WEIGHTS: the caller guarantees that no kernel still running on
+ * `stream` writes `codes` or `scales` (true for weights quantised before the previous launch); the decode
+ * GEMV is then launched with programmatic dependent launch and starts streaming weights while the previous
+ * kernel finishes (x and y still wait for it).  Replaces the same reference call sites as lb_linear; the
+ * overlap itself has no reference counterpart. */
+int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+                 const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+                 unsigned flags, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- multi-GPU */
 

@@ -123,3 +123,30 @@ def test_large_activation_rows_are_exact_after_power_of_two_rescale(cuda):
     ref = O.linear_ref(xg, Wd)
     for r in range(4):
         _check(yg[r:r + 1], ref[r:r + 1])
+
+
+def test_static_weight_overlap_waits_for_the_activations(cuda):
+    """With LB_LINEAR_STATIC_WEIGHTS the GEMV starts streaming weights before the previous kernel ends; the
+    activations written by that previous kernel must still be the ones used."""
+    import torch
+    from apsi_b200 import kernels as Kn
+    from apsi_b200._lib import FMT_INT4_G128
+    g = torch.Generator(device=cuda)
+    g.manual_seed(21)
+    N, K = 11008, 4096
+    W = torch.randn((N, K), generator=g, device=cuda) * 0.02
+    codes, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+    base = torch.randn((4, K), generator=g, device=cuda)
+    ref = []
+    for i in range(4):
+        x = (base[i:i + 1] * (i + 1)).to(torch.bfloat16)
+        ref.append(Kn.linear(FMT_INT4_G128, x, codes, s16, N))
+    torch.cuda.synchronize()
+    xs = torch.empty((1, K), dtype=torch.bfloat16, device=cuda)
+    outs = []
+    for i in range(4):
+        torch.mul(base[i:i + 1], i + 1, out=xs.float()) if False else xs.copy_((base[i:i + 1] * (i + 1)))
+        outs.append(Kn.linear(FMT_INT4_G128, xs, codes, s16, N, static_weights=True))
+    torch.cuda.synchronize()
+    for a, b in zip(ref, outs):
+        assert torch.equal(a, b)
