@@ -15,6 +15,7 @@ FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32 = 1, 2, 3, 4
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 DEVERR_WAIT_TIMEOUT = 1
 LINEAR_STATIC_WEIGHTS = 1
+NOALLOC_SCRATCH_BYTES = 16842752
 
 _CODES = {LB_E_ARG: "bad argument", LB_E_ALIGN: "misaligned", LB_E_DEVICE: "device", LB_E_LAUNCH: "launch",
           LB_E_WORKSPACE: "workspace", LB_E_UNSUPPORTED: "unsupported"}
@@ -35,6 +36,7 @@ SIGNATURES = [
     ("lb_linear", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, _P]),
     ("lb_linear_ex", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, ctypes.c_uint, _P]),
     ("lb_interleave_cols", _I, [_P, _I, _I64, _I64, _P, _P]),
+    ("lb_linear_noalloc", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P]),
 ]
 
 

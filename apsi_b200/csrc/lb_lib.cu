@@ -3,3 +3,4 @@
 #include "lb_gemv.cu"
 #include "lb_gemm.cu"
 #include "lb_api.cu"
+#include "lb_noalloc.cu"

@@ -137,6 +137,20 @@ int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes
                  const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
                  unsigned flags, void* stream);
 
+/* Bytes of the fixed device scratch behind lb_linear_noalloc (16 MiB + 64 KiB: the prefill path fits while
+ * lb_linear_workspace_size(fmt, M, N, K) <= this, e.g. M = 2048, K = 4096). */
+#define LB_NOALLOC_SCRATCH_BYTES 16842752
+
+/* lb_linear without a workspace argument, allocating nothing: the prefill path (M > 16) uses one file-scope
+ * device array per device instead (nothing in it needs to start at zero).  For callers that cannot allocate
+ * at the call: engines whose free HBM is all handed to their own pool, loops that must not take the
+ * synchronisation of cudaMalloc/cudaFree, bindings with no device allocator.  Shapes whose workspace exceeds
+ * LB_NOALLOC_SCRATCH_BYTES fail with LB_E_WORKSPACE.  Calls that overlap in time on one device (two streams
+ * or threads) race on the shared scratch; calls in order on one stream are safe.  The first call on a device
+ * looks the scratch address up: make it outside stream capture.  No counterpart in the reference. */
+int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
+                      int64_t N, const void* bias, int accumulate, void* y, int64_t ldy, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- multi-GPU */
 
 /* Reassembles column shards after an all-gather: src [G][M][Nl] (rank-major, bf16) -> dst [M][G*Nl].

@@ -1,0 +1,67 @@
+"""lb_linear_noalloc: the product through the C ABI with the library's fixed device scratch instead of a
+workspace.  The file name sorts last so these run after every other test (and they also pass alone)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from apsi_b200 import _lib, build
+
+TOL_REL_F = 2e-3      # relative Frobenius error of the layer
+TOL_MAX_ABS = 1e-2    # max-abs error as a fraction of max |y|
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_noalloc_rejects_shapes_beyond_the_scratch(lib):
+    fake = ctypes.c_void_p(1 << 20)    # never dereferenced: the size check fails first
+    null = ctypes.c_void_p(0)
+    M, K = 4096, 4096                   # 32 MiB of fp16 activations > LB_NOALLOC_SCRATCH_BYTES
+    rc = lib.lb_linear_noalloc(_lib.FMT_INT4_G128, fake, M, K, fake, fake, 256, null, 0, fake, 256, null)
+    assert rc == _lib.LB_E_WORKSPACE
+    assert b"scratch" in lib.lb_last_error()
+    rc = lib.lb_linear_noalloc(9, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null)
+    assert rc == _lib.LB_E_UNSUPPORTED
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", [_lib.FMT_INT4_G128, _lib.FMT_INT8_ROW])
+@pytest.mark.parametrize("M", [256, 2048, 1])
+def test_noalloc_matches_lb_linear_twice_in_a_row(lib, cuda, fmt, M):
+    import torch
+    from apsi_b200 import kernels
+
+    N, K = 1024, 4096
+    rng = np.random.default_rng(11 + M + fmt)
+    W = torch.from_numpy((rng.standard_normal((N, K)) * 0.02).astype(np.float32)).to(cuda)
+    if fmt == _lib.FMT_INT4_G128:
+        codes, s16, _ = kernels.quant_int4_g128(W, want_scale32=False)
+    else:
+        codes, s16, _ = kernels.quant_int8_rows(W, want_scale32=False)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    nbytes = kernels.linear_workspace_bytes(fmt, M, N, K)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=cuda) if nbytes else None
+    for call in range(2):   # two calls in a row reuse the same scratch
+        x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(cuda).to(torch.bfloat16)
+        y_ref = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+        y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda)
+        _lib.check(lib.lb_linear(fmt, _ptr(x), M, K, _ptr(codes), _ptr(s16), N, None, 0, _ptr(y_ref), N,
+                                 _ptr(ws), nbytes, stream))
+        _lib.check(lib.lb_linear_noalloc(fmt, _ptr(x), M, K, _ptr(codes), _ptr(s16), N, None, 0, _ptr(y), N,
+                                         stream))
+        torch.cuda.synchronize(cuda)
+        a = y.float().cpu().numpy().astype(np.float64)
+        b = y_ref.float().cpu().numpy().astype(np.float64)
+        assert np.isfinite(a).all(), f"call {call}: unwritten outputs"
+        rel = np.linalg.norm(a - b) / np.linalg.norm(b)
+        mab = np.abs(a - b).max() / np.abs(b).max()
+        assert rel <= TOL_REL_F and mab <= TOL_MAX_ABS, f"call {call}: relF {rel:.3e} maxabs {mab:.3e}"
+    assert kernels.device_errors(cuda) == 0
