@@ -66,15 +66,24 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// Waits for the phase with the given parity to complete.  Each try suspends for at most 1 ms; after
-// kWaitTries tries (a few seconds), or at once when *abort is set, it records LB_DEVERR_WAIT_TIMEOUT, sets
-// *abort so every other wait of the CTA returns at once, and returns false.  Callers carry on (their output is
-// invalid), so no CTA barrier is skipped.
-constexpr uint32_t kWaitTries = 4096;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with the given parity to complete.  Each try lets the hardware suspend the thread while
+// the phase is pending; after kWaitLimitNs of wall time (read from the global timer, so the bound does not
+// depend on how long one try suspends), or at once when *abort is set, it records LB_DEVERR_WAIT_TIMEOUT, sets
+// *abort so every other wait of the CTA returns at once, and returns false.  Callers carry on (their output
+// is invalid), so no CTA barrier is skipped.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < kWaitTries; ++i) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < (1u << 30); ++i) {
     if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
     if (*abort) return false;
+    if ((i & 15u) == 15u && global_ns() - t0 > kWaitLimitNs) break;
   }
   *abort = 1;
   atomicOr(&g_dev_errors, 1);
