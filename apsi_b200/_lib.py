@@ -31,6 +31,7 @@ SIGNATURES = [
     ("lb_quant_int4_g128", _I, [_P, _I, _I64, _I64, _P, _P, _P, _P]),
     ("lb_quant_q8_0_g32", _I, [_P, _I, _I64, _I64, _P, _P, _P]),
     ("lb_quant_q4_0_g32", _I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    ("lb_round_g32", _I, [_I, _P, _I, _I64, _I64, _P, _P]),
     ("lb_dequant", _I, [_I, _P, _P, _I, _I64, _I64, _P, _I, _P]),
     ("lb_linear_workspace_size", _I, [_I, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     ("lb_linear", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, _P]),

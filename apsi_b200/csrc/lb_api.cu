@@ -179,6 +179,20 @@ int lb_quant_q4_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t
   return quant_g32(4, w, w_dtype, N, K, words, scale32, stream, "lb_quant_q4_0_g32");
 }
 
+int lb_round_g32(int fmt, const void* w, int w_dtype, int64_t N, int64_t K, float* out, void* stream) {
+  if (fmt != LB_FMT_Q8_0_G32 && fmt != LB_FMT_Q4_0_G32)
+    return fail(LB_E_UNSUPPORTED, "lb_round_g32: format %d is not a g32 format", fmt);
+  int r = check_weight_input(w, w_dtype, N, K, 32, "lb_round_g32");
+  if (r) return r;
+  if (!out) return fail(LB_E_ARG, "lb_round_g32: out is required");
+  if (!aligned(out, 16)) return fail(LB_E_ALIGN, "lb_round_g32: out must be 16-byte aligned");
+  DevInfo* d;
+  if ((r = current(&d))) return r;
+  return launched(launch_round_g32(fmt == LB_FMT_Q8_0_G32 ? 8 : 4, w, w_dtype, N, K, out, d->sms,
+                                   static_cast<cudaStream_t>(stream)),
+                  "lb_round_g32");
+}
+
 int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, int64_t N, int64_t K, void* out,
                int out_dtype, void* stream) {
   if (fmt < LB_FMT_INT8_ROW || fmt > LB_FMT_Q4_0_G32) return fail(LB_E_ARG, "lb_dequant: unknown format %d", fmt);

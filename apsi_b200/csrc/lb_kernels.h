@@ -12,6 +12,8 @@ cudaError_t launch_quant_int8_rows(const void* w, int dt, int64_t N, int64_t K, 
                                    float* s32, int sms, cudaStream_t st);
 cudaError_t launch_quant_g32(int kind, const void* w, int dt, int64_t N, int64_t K, uint32_t* words, float* s32,
                              int sms, cudaStream_t st);
+cudaError_t launch_round_g32(int kind, const void* w, int dt, int64_t N, int64_t K, float* out, int sms,
+                             cudaStream_t st);
 cudaError_t launch_dequant(int fmt, const void* codes, const void* scales, int sf32, int64_t N, int64_t K,
                            void* out, int out_dt, int sms, cudaStream_t st);
 

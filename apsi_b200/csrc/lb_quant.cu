@@ -150,6 +150,36 @@ __global__ void __launch_bounds__(256) quant_int8_rows_kernel(const void* __rest
 // ------------------------------------------------------------------------------------------- ggml g32
 // Four threads per block of 32 values (8 each).  KIND 8: int8, scale = absmax/127; KIND 4: int4,
 // scale = (first value of largest magnitude)/-8, codes stored as q + 8.  float32 arithmetic as qnumpy.
+// Scale of one block of 32 values held 8 per thread by 4 consecutive lanes (sub = lane % 4), float32 as
+// hub_gpu.qnumpy: int8 max|v| / 127; int4 the signed value of the first largest magnitude / -8.
+template <int KIND>
+__device__ __forceinline__ float g32_scale(const float (&v)[8], int sub) {
+  if (KIND == 8) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+    for (int o = 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 4));
+    return __fdiv_rn(m, 127.0f);
+  }
+  // first index of the largest magnitude (numpy argmax), then its signed value
+  float am = -1.f, mv = 0.f;
+  int idx = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float a = fabsf(v[j]);
+    if (a > am) { am = a; mv = v[j]; idx = sub * 8 + j; }
+  }
+#pragma unroll
+  for (int o = 2; o >= 1; o >>= 1) {
+    float oam = __shfl_xor_sync(0xffffffffu, am, o, 4);
+    float omv = __shfl_xor_sync(0xffffffffu, mv, o, 4);
+    int oidx = __shfl_xor_sync(0xffffffffu, idx, o, 4);
+    if (oam > am || (oam == am && oidx < idx)) { am = oam; mv = omv; idx = oidx; }
+  }
+  return __fdiv_rn(mv, -8.0f);
+}
+
 template <int DT, int KIND>
 __global__ void __launch_bounds__(256) quant_g32_kernel(const void* __restrict__ w, int64_t nblocks,
                                                         uint32_t* __restrict__ words,
@@ -160,32 +190,7 @@ __global__ void __launch_bounds__(256) quant_g32_kernel(const void* __restrict__
   for (; b < nblocks; b += bstride) {
     float v[8];
     load_w8<DT>(w, b * 32 + sub * 8, v);
-    float sc;
-    if (KIND == 8) {
-      float m = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
-#pragma unroll
-      for (int o = 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 4));
-      sc = __fdiv_rn(m, 127.0f);
-    } else {
-      // first index of the largest magnitude (numpy argmax), then its signed value
-      float am = -1.f, mv = 0.f;
-      int idx = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float a = fabsf(v[j]);
-        if (a > am) { am = a; mv = v[j]; idx = sub * 8 + j; }
-      }
-#pragma unroll
-      for (int o = 2; o >= 1; o >>= 1) {
-        float oam = __shfl_xor_sync(0xffffffffu, am, o, 4);
-        float omv = __shfl_xor_sync(0xffffffffu, mv, o, 4);
-        int oidx = __shfl_xor_sync(0xffffffffu, idx, o, 4);
-        if (oam > am || (oam == am && oidx < idx)) { am = oam; mv = omv; idx = oidx; }
-      }
-      sc = __fdiv_rn(mv, -8.0f);
-    }
+    const float sc = g32_scale<KIND>(v, sub);
     const float inv = (sc != 0.f) ? __fdiv_rn(1.0f, sc) : 0.f;
     uint32_t out0 = 0, out1 = 0;
 #pragma unroll
@@ -207,6 +212,30 @@ __global__ void __launch_bounds__(256) quant_g32_kernel(const void* __restrict__
       words[b * 4 + sub] = out0;
     }
     if (sub == 0) scale32[b] = sc;
+  }
+}
+
+// lowbit.round_weights in one pass (apsi/lowbit.py:37-50 with hub_gpu.qnumpy): out = clip(rint(v * inv), lo,
+// hi) * scale in float32, so a value that rounds to zero keeps its sign exactly as the reference's float
+// arithmetic does (integer codes would lose it).
+template <int DT, int KIND>
+__global__ void __launch_bounds__(256) round_g32_kernel(const void* __restrict__ w, int64_t nblocks,
+                                                        float* __restrict__ out) {
+  const int sub = threadIdx.x & 3;
+  int64_t b = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 2;
+  const int64_t bstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 2;
+  for (; b < nblocks; b += bstride) {
+    float v[8];
+    load_w8<DT>(w, b * 32 + sub * 8, v);
+    const float sc = g32_scale<KIND>(v, sub);
+    const float inv = (sc != 0.f) ? __fdiv_rn(1.0f, sc) : 0.f;
+    const float lo = KIND == 8 ? -127.f : -8.f, hi = KIND == 8 ? 127.f : 7.f;
+    float d[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = __fmul_rn(fminf(fmaxf(rintf(__fmul_rn(v[j], inv)), lo), hi), sc);
+    float4* o = reinterpret_cast<float4*>(out + b * 32 + sub * 8);
+    o[0] = make_float4(d[0], d[1], d[2], d[3]);
+    o[1] = make_float4(d[4], d[5], d[6], d[7]);
   }
 }
 
@@ -313,6 +342,20 @@ cudaError_t launch_quant_g32(int kind, const void* w, int dt, int64_t N, int64_t
   } else {
     if (dt == 0) quant_g32_kernel<0, 4><<<grid, 256, 0, st>>>(w, nb, words, s32);
     else quant_g32_kernel<1, 4><<<grid, 256, 0, st>>>(w, nb, words, s32);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_round_g32(int kind, const void* w, int dt, int64_t N, int64_t K, float* out, int sms,
+                             cudaStream_t st) {
+  const int64_t nb = N * (K / 32);
+  const int grid = grid_for(nb * 4, sms);
+  if (kind == 8) {
+    if (dt == 0) round_g32_kernel<0, 8><<<grid, 256, 0, st>>>(w, nb, out);
+    else round_g32_kernel<1, 8><<<grid, 256, 0, st>>>(w, nb, out);
+  } else {
+    if (dt == 0) round_g32_kernel<0, 4><<<grid, 256, 0, st>>>(w, nb, out);
+    else round_g32_kernel<1, 4><<<grid, 256, 0, st>>>(w, nb, out);
   }
   return cudaGetLastError();
 }

@@ -11,7 +11,7 @@ import torch
 from . import _lib
 from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F32, DT_BF16, LowbitError
 
-__all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "dequant", "linear",
+__all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "round_g32", "dequant", "linear",
            "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
            "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError"]
 
@@ -86,6 +86,17 @@ def quant_q4_0_g32(w):
     with torch.cuda.device(w.device):
         _lib.call("lb_quant_q4_0_g32", _ptr(w), _weight_dtype(w), N, K, _ptr(words), _ptr(s32), _stream(w.device))
     return words, s32
+
+
+def round_g32(w, fmt):
+    """lowbit.round_weights on rows: [N, K] float32 values clip(rint(w * inv)) * scale per block of 32 along K
+    (fmt FMT_Q8_0_G32 or FMT_Q4_0_G32), signed zeros as the reference's float arithmetic gives them."""
+    _need_cuda(w, "w")
+    N, K = w.shape
+    out = torch.empty((N, K), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        _lib.call("lb_round_g32", fmt, _ptr(w), _weight_dtype(w), N, K, _ptr(out), _stream(w.device))
+    return out
 
 
 # ------------------------------------------------------------------------------------------------ dequantise

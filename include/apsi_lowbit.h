@@ -101,6 +101,12 @@ int lb_quant_q4_0_g32(const void* w, int w_dtype, int64_t N, int64_t K, uint32_t
 
 /* ---------------------------------------------------------------------------------------------- dequantise */
 
+/* The g32 rounding in one pass: out[N, K] (float32, 16-byte aligned) = clip(rint(w * inv), lo, hi) * scale
+ * per block of 32 along K, with hub_gpu.qnumpy's float32 scale (fmt LB_FMT_Q8_0_G32 or LB_FMT_Q4_0_G32).
+ * Bit-exact with lowbit.round_weights / round_weights_torch on the rows, signed zeros included
+ * (apsi/lowbit.py:37-50, 62-94; apsi/hub_gpu.py:1215-1241). */
+int lb_round_g32(int fmt, const void* w, int w_dtype, int64_t N, int64_t K, float* out, void* stream);
+
 /* out[N, K] = code * scale in `out_dtype` (LB_DT_F32: the exact float32 product, as precision.dequantize;
  * LB_DT_BF16: that product rounded to nearest even).  `scales` are `scale_dtype`: LB_DT_F16 (the stored
  * binary16 scales) or LB_DT_F32 (the reference's float32 scales, which makes the result bit-exact with

@@ -25,7 +25,7 @@ __all__ = [
     "bf16_round", "bf16_to_f32", "f32_to_bf16_bits", "scale_for_segments", "quant_segments", "pack4", "unpack4",
     "quant_int8_rows", "quant_int4_g128", "dequant_int8_rows", "dequant_int4_g128", "linear_ref",
     "qnumpy_g32", "pack_q4_0_words", "pack_q8_0_words", "dequant_g32", "rel_frobenius", "max_abs_ratio",
-    "make_config_inputs", "qmatmul_dequant_reference",
+    "make_config_inputs", "qmatmul_dequant_reference", "round_weights_g32",
 ]
 
 
@@ -205,6 +205,23 @@ def dequant_g32(q, sc):
 
 
 # ------------------------------------------------------------------------------------------- error metrics
+def round_weights_g32(a, kind):
+    """apsi/lowbit.py:37-50 (``round_weights``) for "int8" / "int4": a [..., in, out] weight read as rows
+    [out, in*...], each row padded with zeros to a multiple of 32, rounded with qnumpy_g32, multiplied back by
+    the block scale (float32), the padding dropped and the result returned in a's shape and dtype."""
+    a = np.asarray(a)
+    if a.ndim < 2 or a.dtype.kind != "f":
+        return a
+    n_in, n_out = int(np.prod(a.shape[:-1])), int(a.shape[-1])
+    rows = np.asarray(a, np.float32).reshape(n_in, n_out).T
+    pad = (-n_in) % 32
+    if pad:
+        rows = np.concatenate([rows, np.zeros((n_out, pad), np.float32)], axis=1)
+    q, sc = qnumpy_g32(rows, kind)
+    d = dequant_g32(q, sc)[:, :n_in]
+    return d.T.reshape(a.shape).astype(a.dtype)
+
+
 def rel_frobenius(y, ref):
     ref = np.asarray(ref, np.float64)
     d = np.asarray(y, np.float64) - ref

@@ -25,6 +25,11 @@ def _reference():
     return precision, hub_gpu
 
 
+def _reference_lowbit():
+    from apsi import lowbit  # noqa: E402  (after _reference() put the reference on the path)
+    return lowbit
+
+
 def _adversarial_rows(rng, K, qmax):
     """Rows whose quotients land exactly on, and one ulp beside, half-integers."""
     rows = []
@@ -100,6 +105,18 @@ def main():
         qv, sc = hub_gpu.qnumpy(Wg, kind)
         out[f"wg_{kind}_q"] = np.asarray(qv, np.float32)
         out[f"wg_{kind}_scale"] = np.asarray(sc, np.float32)
+
+    # ---- lowbit.round_weights (rows = outputs, blocks of 32 along the inputs, padded) on an [in, out] weight
+    # whose input size is not a multiple of 32, with tiny, zero and exactly representable columns
+    lowbit = _reference_lowbit()
+    n_in, n_out = 70, 24
+    Wr = (rng.standard_normal((n_in, n_out)) * 0.05).astype(np.float32)
+    Wr[:, 3] *= 1e-4
+    Wr[:, 5] = 0.0
+    Wr[:, 7] = np.tile(np.array([0.5, -0.25, 1.75, 7.0, -8.0], np.float32), 14)[:n_in]
+    out["rw_in"] = Wr
+    for kind in ("int8", "int4"):
+        out[f"rw_{kind}"] = np.asarray(lowbit.round_weights(Wr, kind), np.float32)
 
     path = os.path.join(HERE, "lowbit_golden.npz")
     np.savez_compressed(path, **out)

@@ -63,3 +63,9 @@ def test_error_metrics():
     ref = np.array([[1.0, -2.0, 4.0]])
     assert O.rel_frobenius(ref, ref) == 0.0
     assert abs(O.max_abs_ratio(ref + np.array([[0, 0, 0.04]]), ref) - 0.01) < 1e-12
+
+
+def test_round_weights_matches_reference_lowbit(golden):
+    for kind in ("int8", "int4"):
+        got = O.round_weights_g32(golden["rw_in"], kind)
+        assert np.array_equal(got.view(np.uint32), golden[f"rw_{kind}"].view(np.uint32)), kind
