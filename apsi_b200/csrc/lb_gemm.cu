@@ -1,24 +1,24 @@
 // Prefill-regime product (M > 16 tokens) on the 5th-generation tensor cores (tcgen05).
 //
-//   D[n, m] = sum_k deq(W)[n, k] * x[m, k]      A = W tile (128 weight rows)   in TENSOR MEMORY
+//   D[n, m] = sum_k deq(W)[n, k] * x[m, k]      A = W tile (128 weight rows)   in shared memory (dequantised)
 //                                                B = x tile (BN tokens)         in shared memory (TMA, SW128)
-//                                                D = fp32 accumulators          in TENSOR MEMORY
+//                                                D = fp32 accumulators          in TENSOR MEMORY, two of them
 //
-// Why A lives in tensor memory: the weights arrive as 4/8-bit codes and must be expanded before the MMA.
-// Writing the expanded tile to shared memory and reading it back through the MMA would double the shared-
-// memory traffic of the weight operand on top of the activation stream; tcgen05.st puts it in TMEM instead,
-// so shared memory only carries the TMA-staged activations and the small raw code tiles.
+// The weights arrive as 4/8-bit codes (TMA, a few KB per stage) and eight dequantising warps expand them into
+// the fp16 A tile in shared memory, in the same 128-byte swizzled K-major layout the TMA gives the activation
+// tile, so one `tcgen05.mma` (both operands from shared memory) consumes them.  Tensor memory then only holds
+// accumulators: two of BN columns each, so four epilogue warps drain tile i while the MMAs of tile i + 1 run.
 //
 // Operands are fp16: codes are exact in fp16 and int4 weights are fp16(q * s16) with a single rounding
 // (relative error <= 2^-11); the activations are converted once by prep_x_kernel with a per-row power-of-two
 // factor so the conversion is exact (bf16 mantissas fit in fp16) and cannot overflow; the factor is undone in
 // the epilogue.  int8 rows keep exact codes and apply the row scale in float32 in the epilogue.
 //
-// Roles (10 warps, persistent over tiles):
-//   warp 0      TMA producer: activation tile (BN x 64 fp16, SW128) + raw code tile (128 rows) per stage
-//   warp 1      TMEM allocator and MMA issuer (one thread): 4 x tcgen05.mma K=16 per stage, commit -> mbarrier
-//   warps 2..9  dequantise one quarter of the rows x one half of the stage's K into TMEM (tcgen05.st), then
-//               run the tile epilogue (tcgen05.ld -> scale -> bf16 -> global)
+// Roles (14 warps, persistent over tiles):
+//   warp 0        TMA producer: activation tile (BN x 64 fp16, SW128) + raw code tile (128 rows) per stage
+//   warp 1        TMEM allocator and MMA issuer (one thread): 4 x tcgen05.mma K=16 per stage, commit -> mbarrier
+//   warps 2..9    dequantise one row x one half of the stage's K into the A tile (st.shared + proxy fence)
+//   warps 10..13  epilogue: tcgen05.ld -> scale / bias / accumulate -> bf16 -> global
 // All mbarrier waits are bounded (lb::mbar_wait); a timeout sets the device error word and the CTA drains.
 #include <cuda.h>
 #include "lb_common.cuh"
@@ -28,9 +28,12 @@ namespace lb {
 
 namespace gemm {
 constexpr int BM = 128;     // weight rows per tile = TMEM lanes
-constexpr int BK = 64;      // K values per stage
+constexpr int BK = 64;      // K values per stage (128 bytes of fp16: one SW128 row)
 constexpr int STAGES = 4;
-constexpr int THREADS = 320;
+constexpr int DQ_WARPS = 8;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (2 + DQ_WARPS + EPI_WARPS) * 32;   // TMA, MMA, dequantisers, epilogue
+constexpr int A_STAGE = BM * BK * 2;                       // 16 KB of fp16 weights per stage
 }  // namespace gemm
 
 struct GemmParams {
@@ -52,7 +55,7 @@ struct GemmCfg {
 template <int BN>
 struct GemmSmem {
   static constexpr int X_STAGE = BN * 128;
-  static constexpr int TMEM_COLS = (BN + gemm::STAGES * 32 <= 256) ? 256 : 512;
+  static constexpr int TMEM_COLS = (2 * BN <= 128) ? 128 : (2 * BN <= 256 ? 256 : 512);   // two accumulators
 };
 
 __device__ __forceinline__ uint16_t f32_to_bf16_bits_g(float f) {
@@ -158,6 +161,18 @@ __device__ __forceinline__ void deq_int8_f16(const uint4 a, const uint4 b, uint3
 }
 
 // ------------------------------------------------------------------------------------------- the GEMM
+// A (the dequantised weights) and B (the activations) both come from shared memory in the 128-byte swizzled
+// K-major layout; the fp32 accumulators live in tensor memory, two of them, so the epilogue of one tile
+// overlaps the main loop of the next.
+__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 template <int FMT, int BN>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -168,16 +183,17 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
   // 1024-align the carve-out (SW128 atoms)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
-  uint8_t* xs = smem;                                          // STAGES x X_STAGE
-  uint8_t* raw = xs + STAGES * Sm::X_STAGE;                    // STAGES x RAW_STAGE
+  uint8_t* xs = smem;                                          // STAGES x X_STAGE  (TMA, SW128)
+  uint8_t* as = xs + STAGES * Sm::X_STAGE;                     // STAGES x A_STAGE  (dequantisers, SW128)
+  uint8_t* raw = as + STAGES * A_STAGE;                        // STAGES x RAW_STAGE (TMA)
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + STAGES * Cfg::RAW_STAGE);
   uint64_t* full_x = bars;
   uint64_t* full_w = bars + STAGES;
   uint64_t* a_full = bars + 2 * STAGES;
   uint64_t* empty = bars + 3 * STAGES;
-  uint64_t* acc_full = bars + 4 * STAGES;
-  uint64_t* acc_empty = acc_full + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* acc_full = bars + 4 * STAGES;                      // [2]
+  uint64_t* acc_empty = acc_full + 2;                          // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -187,11 +203,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_x[s], 1);
       mbar_init(&full_w[s], 1);
-      mbar_init(&a_full[s], 8);
+      mbar_init(&a_full[s], DQ_WARPS);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_x);
@@ -229,8 +247,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
       uint32_t it = 0, tcount = 0;
       for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
-        if (tcount > 0) mbar_wait(acc_empty, (tcount - 1) & 1, abort_v);
+        const uint32_t b = tcount & 1;
+        if (tcount >= 2) mbar_wait(&acc_empty[b], ((tcount >> 1) - 1) & 1, abort_v);   // epilogue of tile - 2
         tc_fence_after();
+        const uint32_t d_tmem = tmem + b * BN;
         for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
           const uint32_t slot = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -238,26 +258,25 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           mbar_wait(&a_full[slot], ph, abort_v);
           tc_fence_after();
           const uint32_t xaddr = smem_u32(xs + slot * Sm::X_STAGE);
+          const uint32_t aaddr = smem_u32(as + slot * A_STAGE);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t bdesc = smem_desc_sw128(xaddr + kk * 32);
-            const uint32_t a_tmem = tmem + BN + slot * 32 + kk * 8;
-            tc_mma_ts(tmem, a_tmem, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_ss(d_tmem, smem_desc_sw128(aaddr + kk * 32), smem_desc_sw128(xaddr + kk * 32), idesc,
+                      (ks > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&empty[slot]);
         }
-        tc_commit(acc_full);
+        tc_commit(&acc_full[b]);
       }
     }
-  } else {
-    // ------------------------------------------------------------------ dequantise + epilogue
-    const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int h = (warp - 2) >> 2;          // K half of each stage
-    const int rloc = q * 32 + lane;         // row within the tile
-    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    uint32_t it = 0, tcount = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
-      const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+  } else if (warp < 2 + DQ_WARPS) {
+    // ------------------------------------------------------------------ dequantise into shared memory
+    const int d = threadIdx.x - 64;         // 0..255
+    const int rloc = d & (BM - 1);          // row within the tile
+    const int h = d >> 7;                   // K half of each stage (32 values = 64 bytes of fp16)
+    const uint32_t arow = static_cast<uint32_t>((rloc >> 3) * 1024 + (rloc & 7) * 128);
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
+      const int mb = tile / p.n_blocks;
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
       for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
@@ -270,7 +289,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           s2 = *reinterpret_cast<const uint32_t*>(&sp);
         }
         mbar_wait(&full_w[slot], ph, abort_v);
-        if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
+        if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);   // MMA done with A
         uint32_t o[16];
         const uint32_t rbase = smem_u32(raw + slot * Cfg::RAW_STAGE) + rloc * Cfg::RAW_ROW;
         if (FMT == 2) {
@@ -284,29 +303,47 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           const uint4 b = lds_v4(rbase + 16 * ((2 * h + 1) ^ sw));
           deq_int8_f16(a, b, o);
         }
-        tmem_st_x16(tmem + lane_addr + BN + slot * 32 + 16 * h, o);
-        tc_wait_st();
-        tc_fence_before();
+        // row rloc, 16-byte chunks 4h .. 4h+3 of its 128-byte K row, 128-byte swizzle: chunk ^= row % 8
+        const uint32_t abase = smem_u32(as + slot * A_STAGE) + arow;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t c = static_cast<uint32_t>((4 * h + j) ^ (rloc & 7));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(abase + c * 16), "r"(o[4 * j]),
+                       "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
+                       : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[slot]);
       }
-      // ---------------------------------------------------------------- epilogue of this tile
-      mbar_wait(acc_full, tcount & 1, abort_v);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue: TMEM -> bf16 outputs
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int rloc = q * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
+      const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+      const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
+      const int64_t rowc = row < p.N ? row : p.N - 1;
+      const uint32_t b = tcount & 1;
+      mbar_wait(&acc_full[b], (tcount >> 1) & 1, abort_v);
       tc_fence_after();
       float rs = 1.f, bias = 0.f;
       if (FMT == 1) rs = __half2float(p.s16[rowc]);
       if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
       const bool row_ok = row < p.N;
 #pragma unroll 1
-      for (int c0 = h * (BN / 2); c0 < (h + 1) * (BN / 2); c0 += 16) {
-        uint32_t d[16];
-        tmem_ld_x16(tmem + lane_addr + c0, d);
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t dv[16];
+        tmem_ld_x16(tmem + lane_addr + b * BN + c0, dv);
         tc_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int64_t tok = static_cast<int64_t>(nb) * BN + c0 + j;
           if (row_ok && tok < p.M) {
-            float v = __uint_as_float(d[j]) * (p.tokscale[tok] * rs);
+            float v = __uint_as_float(dv[j]) * (p.tokscale[tok] * rs);
             v += bias;
             uint16_t* yp = p.y + tok * p.ldy + row;
             if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
@@ -316,7 +353,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
 
@@ -349,7 +386,7 @@ static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256)
 
 size_t gemm_smem_bytes(int fmt, int bn) {
   const int raw = (fmt == 2) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
-  return 1024 + static_cast<size_t>(gemm::STAGES) * (bn * 128 + raw) + 256;
+  return 1024 + static_cast<size_t>(gemm::STAGES) * (bn * 128 + gemm::A_STAGE + raw) + 256;
 }
 
 size_t gemm_workspace_bytes(int64_t M, int64_t K) {
