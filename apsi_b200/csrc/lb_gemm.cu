@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict_
   if (row >= M) return;
   const uint16_t* xr = x + row * K;
   float m = 0.f;
+#pragma unroll 8
   for (int64_t k = lane * 8; k < K; k += 256) {
     uint4 v = ldg_nc_v4(xr + k);
     uint32_t r[4] = {v.x, v.y, v.z, v.w};
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict_
   const float down = ldexpf(1.0f, -e);
   if (lane == 0) tokscale[row] = ldexpf(1.0f, e);
   uint16_t* out = x16 + row * K;
+#pragma unroll 8
   for (int64_t k = lane * 8; k < K; k += 256) {
     uint4 v = ldg_nc_v4(xr + k);
     uint32_t r[4] = {v.x, v.y, v.z, v.w};
@@ -279,14 +281,27 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       const int mb = tile / p.n_blocks;
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
+      // int4 scales of this row, one group of 128 per two stages, fetched four groups ahead through a small
+      // register queue so their latency does not stall a stage
+      static_assert(BK * 2 == 128, "two stages per scale group");
+      const int ng = static_cast<int>(p.K / 128);
+      const unsigned short* srow = reinterpret_cast<const unsigned short*>(p.s16) + rowc * ng;
+      unsigned short sq0 = 0, sq1 = 0, sq2 = 0, sq3 = 0;
+      if (FMT == 2) {
+        sq0 = __ldg(srow);
+        if (ng > 1) sq1 = __ldg(srow + 1);
+        if (ng > 2) sq2 = __ldg(srow + 2);
+        if (ng > 3) sq3 = __ldg(srow + 3);
+      }
+      uint32_t s2 = 0;
       for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
         const uint32_t slot = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        uint32_t s2 = 0;
-        if (FMT == 2) {
-          const __half s = p.s16[rowc * (p.K / 128) + (ks * BK) / 128];
-          const __half2 sp = __halves2half2(s, s);
-          s2 = *reinterpret_cast<const uint32_t*>(&sp);
+        if (FMT == 2 && (ks & 1) == 0) {
+          const int gi = ks >> 1;
+          s2 = static_cast<uint32_t>(sq0) * 0x00010001u;
+          sq0 = sq1; sq1 = sq2; sq2 = sq3;
+          if (gi + 4 < ng) sq3 = __ldg(srow + gi + 4);
         }
         mbar_wait(&full_w[slot], ph, abort_v);
         if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);   // MMA done with A
