@@ -5,22 +5,23 @@
 // unit is 128 values = one scale group; int8: 64 values).
 //
 // Roles per CTA: one producer warp streams the CTA's items, in order, through a shared-memory ring with TMA
-// bulk copies (cp.async.bulk, one 2 KB copy per row -- smaller copies do not reach full HBM bandwidth) and
-// full / empty mbarriers per slot.  The consumer warps form G groups of four; item q belongs to group q % G,
-// so G items are multiplied at once.  Each group owns every G-th slot of the ring (the ring holds a multiple
-// of G slots), so a slot is always filled for, and read by, one group in item order and a parity wait can
-// never see a phase that belongs to another item.  A warp copies all of its codes of an item into registers
-// and releases the slot before multiplying.  Within an item, warp w of the group takes units w, w + 4, ...
-// (eight units), in order; the four warp partials are added in warp order after one group barrier.
+// bulk copies (cp.async.bulk, one 2 KB copy per row -- smaller copies do not reach full HBM bandwidth -- with
+// an evict-first L2 policy, as the weights are read once) and full / empty mbarriers per slot.  The consumer
+// warps form G groups of four; item q belongs to group q % G, so G items are multiplied at once.  Each group
+// owns every G-th slot of the ring (the ring holds a multiple of G slots), so a slot is always filled for, and
+// read by, one group in item order and a parity wait can never see a phase that belongs to another item.  A
+// warp copies all of its codes of an item into registers and releases the slot before multiplying.  Within an
+// item, warp w of the group takes units w, w + 4, ... (eight units), in order; the four warp partials are
+// added in warp order after one group barrier.
 //
-// Activations are converted once per CTA into shared memory as fp16, in the order of the tensor-core B
-// fragments, with a power-of-two factor per (token, K range) so the bf16 -> fp16 conversion is exact.  Codes
-// are dequantised in registers with one LOP3 per pair: the code, made offset-binary by an XOR folded into the
-// LOP3, lands in the mantissa of 1024 in fp16 (int4 nibbles at bits 4-7 land as 1024 + 16 n), which is exact.
-// The offsets are not removed per code: each unit's tensor-core sums are split in two classes of K positions
-// (even / odd nibbles), the odd class is scaled by 1/16, and one float per (token, unit),
-// 1032 * sum(x even) + 72 * sum(x odd) (int8: 1152 * sum(x)), computed while staging x, is subtracted.
-// Products accumulate in float32 (m16n8k16 mma.sync); the fp16 scale of each 128-value group multiplies the
+// int4 runs on the bf16 tensor path: a code q becomes the bf16 value 136 + q (= 128 + (q + 8), 8 significant
+// bits, exact) with one LOP3 per pair -- the XOR that makes the nibble offset-binary is folded into it -- and
+// the activations are used as they are, bf16 in the B-fragment order, so every product is exact in the fp32
+// accumulation.  The offset is not removed per code: one float per (token, unit), 136 * sum(x), computed while
+// staging x, starts the accumulation negated.  int8 runs on the fp16 path: codes 1024 + (q + 128) are exact in
+// fp16, the activations are converted once per CTA to fp16 with a power-of-two factor per (token, K range) so
+// the conversion is exact, and 1152 * sum(x) is the offset correction.  Products accumulate in float32
+// (m16n8k16 mma.sync, two independent chains per unit); the fp16 scale of each 128-value group multiplies the
 // unit's float32 partial (int8: the row scale multiplies the final sum).
 //
 // Fixed summation structure: the partial of an item is always formed by the same four-warp split, and the
@@ -85,15 +86,23 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// int4: one word (8 codes, two's complement nibbles) -> four fp16 pairs with n = q + 8:
-// P0 = 1024 + (n0, n4), P1 = 1024 + 16 (n1, n5), P2 = 1024 + (n2, n6), P3 = 1024 + 16 (n3, n7).
-__device__ __forceinline__ void deq4_word(uint32_t w, uint32_t (&P)[4]) {
-  const uint32_t w8 = w >> 8;
-  P[0] = lop3_and_xor_or(w, 0x000F000Fu, 0x64086408u);
-  P[1] = lop3_and_xor_or(w, 0x00F000F0u, 0x64806480u);
-  P[2] = lop3_and_xor_or(w8, 0x000F000Fu, 0x64086408u);
-  P[3] = lop3_and_xor_or(w8, 0x00F000F0u, 0x64806480u);
+// m16n8k16 bf16 tensor-core product, fp32 accumulate: d += a * b.
+__device__ __forceinline__ void mma_bf16_16816_acc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// int4 in bf16: one word (8 codes) -> four bf16 pairs 128 + n with n = q + 8 (exact: 8 significant bits):
+// P0 = (n0, n4), P1 = (n1, n5), P2 = (n2, n6), P3 = (n3, n7).
+__device__ __forceinline__ void deq4_word_bf16(uint32_t w, uint32_t (&P)[4]) {
+  P[0] = lop3_and_xor_or(w, 0x000F000Fu, 0x43084308u);
+  P[1] = lop3_and_xor_or(w >> 4, 0x000F000Fu, 0x43084308u);
+  P[2] = lop3_and_xor_or(w >> 8, 0x000F000Fu, 0x43084308u);
+  P[3] = lop3_and_xor_or(w >> 12, 0x000F000Fu, 0x43084308u);
+}
+
 // int8: one word (4 codes) -> two fp16 pairs 1024 + (n0, n2), 1024 + (n1, n3) with n = q + 128.
 __device__ __forceinline__ void deq8_word(uint32_t w, uint32_t& q02, uint32_t& q13) {
   const uint32_t v = w ^ 0x80808080u;
@@ -115,17 +124,18 @@ __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const
     c1[t][0] = c1[t][1] = c1[t][2] = c1[t][3] = 0.f;
   }
   if (FMT == 2) {
+    // bf16 codes 136 + q against the bf16 activations: exact products, two independent chains
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t P0[4], P8[4];
-      deq4_word(W0[i], P0);
-      deq4_word(W8[i], P8);
-      const uint32_t ae[4] = {P0[0], P8[0], P0[2], P8[2]};   // even nibbles: (0,4) | (2,6)
-      const uint32_t ao[4] = {P0[1], P8[1], P0[3], P8[3]};   // odd nibbles:  (1,5) | (3,7), times 16
+      deq4_word_bf16(W0[i], P0);
+      deq4_word_bf16(W8[i], P8);
+      const uint32_t ae[4] = {P0[0], P8[0], P0[2], P8[2]};   // nibbles (0,4) | (2,6)
+      const uint32_t ao[4] = {P0[1], P8[1], P0[3], P8[3]};   // nibbles (1,5) | (3,7)
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        mma_f16_16816(c0[t], ae, B[t][4 * i + 0], B[t][4 * i + 1]);
-        mma_f16_16816(c1[t], ao, B[t][4 * i + 2], B[t][4 * i + 3]);
+        mma_bf16_16816_acc(c0[t], ae, B[t][4 * i + 0], B[t][4 * i + 1]);
+        mma_bf16_16816_acc(c1[t], ao, B[t][4 * i + 2], B[t][4 * i + 3]);
       }
     }
   } else {
@@ -141,7 +151,7 @@ __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const
       }
     }
   }
-  const float k1 = (FMT == 2) ? 0.0625f : 1.0f;
+  const float k1 = 1.0f;
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
     acc[t][0] = fmaf(fmaf(c1[t][0], k1, c0[t][0]), s0, acc[t][0]);
@@ -252,6 +262,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     // ------------------------------------------------------------------ producer warp
     // lane 0 registers the byte count, lanes 0..15 copy one row each; the weights do not depend on earlier
     // kernels, so streaming starts before griddepcontrol.wait
+    const uint64_t wpol = l2_policy_evict_first();   // the weights are read once
     for (int q = 0; q < nq && !*abort_v; ++q) {
       const int k = q / nloc, i = q - k * nloc;
       const int64_t row0 = static_cast<int64_t>(cid + k * p.C) * RB;
@@ -263,8 +274,9 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], bytes_row * rows_valid);
       __syncwarp();
       if (lane < rows_valid)
-        bulk_g2s(ring + slot * STAGE_BYTES + lane * ROW_STRIDE,
-                 p.w + (row0 + lane) * row_bytes + static_cast<int64_t>(u0) * UNIT, bytes_row, &full_bar[slot]);
+        bulk_g2s_hint(ring + slot * STAGE_BYTES + lane * ROW_STRIDE,
+                      p.w + (row0 + lane) * row_bytes + static_cast<int64_t>(u0) * UNIT, bytes_row, &full_bar[slot],
+                      wpol);
     }
   } else {
     // ------------------------------------------------------------------ consumers
@@ -294,86 +306,122 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
         else { u = jj >> 3; cc = (jj >> 1) & 3; vv = jj & 1; }
         return xs + t * L.token_stride + (il * RANGE_UNITS + u) * XU + vv * 64 + cc * 16;
       };
+      if (FMT == 2) {
+        // int4: the bf16 activations are used as they are (the bf16 products are exact), permuted into the
+        // B-fragment order; one pass, the offset correction 136 * sum(x) per (token, unit)
+        for (int base = 0; base < nch; base += CT * XB) {
+          uint4 v[XB];
+#pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            int t, il, jj, r;
+            v[b] = make_uint4(0u, 0u, 0u, 0u);
+            if (locate(base + b * CT + ctid, t, il, jj, r))
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+          }
+#pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            const int q = base + b * CT + ctid;
+            int t, il, jj, r;
+            const bool ok = locate(q, t, il, jj, r);
+            float sum = 0.f;
+            if (ok) {
+              // (x0,x4) (x2,x6) (x1,x5) (x3,x7), matching the code pairs of deq4_word_bf16
+              const uint32_t o0 = prmt(v[b].x, v[b].z, 0x5410u), o1 = prmt(v[b].y, v[b].w, 0x5410u);
+              const uint32_t o2 = prmt(v[b].x, v[b].z, 0x7632u), o3 = prmt(v[b].y, v[b].w, 0x7632u);
+              *reinterpret_cast<uint4*>(slot_of(t, il, jj)) = make_uint4(o0, o1, o2, o3);
+              auto lo = [](uint32_t u) { return __uint_as_float(u << 16); };
+              auto hi = [](uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); };
+              sum = ((lo(o0) + hi(o0)) + (lo(o1) + hi(o1))) + ((lo(o2) + hi(o2)) + (lo(o3) + hi(o3)));
+              if (jj == 0) xsc[t * MAX_RANGES + r] = 1.0f;
+            }
+#pragma unroll
+            for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
+            if (ok && (jj % CPU) == 0) corr[t * units_staged + il * RANGE_UNITS + jj / CPU] = 136.f * sum;
+          }
+        }
+        named_sync(1, CT);
+      } else {
       for (int base = 0; base < nch; base += CT * XB) {        // pass 1
-        uint4 v[XB];
-#pragma unroll
-        for (int b = 0; b < XB; ++b) {
+          uint4 v[XB];
+  #pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            int t, il, jj, r;
+            v[b] = make_uint4(0u, 0u, 0u, 0u);
+            if (locate(base + b * CT + ctid, t, il, jj, r))
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+          }
+  #pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            const int q = base + b * CT + ctid;
+            int t, il, jj, r;
+            const bool ok = locate(q, t, il, jj, r);
+            if (ok) *reinterpret_cast<uint4*>(slot_of(t, il, jj)) = v[b];
+            const uint32_t rr[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+            float m = 0.f;
+  #pragma unroll
+            for (int e = 0; e < 4; ++e)
+              m = fmaxf(m, fmaxf(fabsf(__uint_as_float(rr[e] << 16)), fabsf(__uint_as_float(rr[e] & 0xFFFF0000u))));
+            // a warp's 32 chunks lie in one (token, range)
+  #pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0 && ok && m > 0.f)   // non-negative floats order like their bit patterns
+              atomicMax(&xmax[t * MAX_RANGES + r], static_cast<int>(__float_as_uint(m)));
+          }
+        }
+        named_sync(1, CT);
+        for (int q = ctid; q < ((nch + 31) & ~31); q += CT) {   // pass 2
+          float se = 0.f, so = 0.f;
           int t, il, jj, r;
-          v[b] = make_uint4(0u, 0u, 0u, 0u);
-          if (locate(base + b * CT + ctid, t, il, jj, r))
-            v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+          const bool valid = locate(q, t, il, jj, r);
+          if (valid) {
+            const float m = __uint_as_float(static_cast<uint32_t>(xmax[t * MAX_RANGES + r]));
+            int e = 0;
+            if (m > 0.f) {
+              int ex;
+              frexpf(m, &ex);
+              e = min(max(ex - 15, -110), 110);               // max |x| * 2^-e in [2^14, 2^15)
+            }
+            if (jj == 0) xsc[t * MAX_RANGES + r] = ldexpf(1.0f, e);
+            const float down = ldexpf(1.0f, -e);
+            uint4* dst = reinterpret_cast<uint4*>(slot_of(t, il, jj));
+            const uint4 v = *dst;
+            const uint32_t rr[4] = {v.x, v.y, v.z, v.w};
+            float f[8];
+  #pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+              f[2 * e2] = __uint_as_float(rr[e2] << 16) * down;
+              f[2 * e2 + 1] = __uint_as_float(rr[e2] & 0xFFFF0000u) * down;
+            }
+            float g8[8];
+            if (FMT == 2) {   // even class (0,4) (2,6), then odd class (1,5) (3,7)
+              g8[0] = f[0]; g8[1] = f[4]; g8[2] = f[2]; g8[3] = f[6]; g8[4] = f[1]; g8[5] = f[5]; g8[6] = f[3]; g8[7] = f[7];
+            } else {          // byte pairs (0,2) (1,3) of each word
+              g8[0] = f[0]; g8[1] = f[2]; g8[2] = f[1]; g8[3] = f[3]; g8[4] = f[4]; g8[5] = f[6]; g8[6] = f[5]; g8[7] = f[7];
+            }
+            uint32_t o[4];
+  #pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+              __half2 h = __floats2half2_rn(g8[2 * e2], g8[2 * e2 + 1]);
+              o[e2] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            // the values are exact in fp16, so the class sums use the converted values
+            se = (g8[0] + g8[1]) + (g8[2] + g8[3]);
+            so = (g8[4] + g8[5]) + (g8[6] + g8[7]);
+            if (FMT == 1) { se += so; so = 0.f; }
+            *dst = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+          // class sums of a unit: its CPU consecutive lanes, fixed shuffle tree
+  #pragma unroll
+          for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) {
+            se += __shfl_xor_sync(0xffffffffu, se, o2);
+            so += __shfl_xor_sync(0xffffffffu, so, o2);
+          }
+          if (valid && (jj % CPU) == 0)
+            corr[t * units_staged + il * RANGE_UNITS + jj / CPU] = (FMT == 2) ? fmaf(1032.f, se, 72.f * so) : 1152.f * se;
         }
-#pragma unroll
-        for (int b = 0; b < XB; ++b) {
-          const int q = base + b * CT + ctid;
-          int t, il, jj, r;
-          const bool ok = locate(q, t, il, jj, r);
-          if (ok) *reinterpret_cast<uint4*>(slot_of(t, il, jj)) = v[b];
-          const uint32_t rr[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
-          float m = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            m = fmaxf(m, fmaxf(fabsf(__uint_as_float(rr[e] << 16)), fabsf(__uint_as_float(rr[e] & 0xFFFF0000u))));
-          // a warp's 32 chunks lie in one (token, range)
-#pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0 && ok && m > 0.f)   // non-negative floats order like their bit patterns
-            atomicMax(&xmax[t * MAX_RANGES + r], static_cast<int>(__float_as_uint(m)));
-        }
+        named_sync(1, CT);
       }
-      named_sync(1, CT);
-      for (int q = ctid; q < ((nch + 31) & ~31); q += CT) {   // pass 2
-        float se = 0.f, so = 0.f;
-        int t, il, jj, r;
-        const bool valid = locate(q, t, il, jj, r);
-        if (valid) {
-          const float m = __uint_as_float(static_cast<uint32_t>(xmax[t * MAX_RANGES + r]));
-          int e = 0;
-          if (m > 0.f) {
-            int ex;
-            frexpf(m, &ex);
-            e = min(max(ex - 15, -110), 110);               // max |x| * 2^-e in [2^14, 2^15)
-          }
-          if (jj == 0) xsc[t * MAX_RANGES + r] = ldexpf(1.0f, e);
-          const float down = ldexpf(1.0f, -e);
-          uint4* dst = reinterpret_cast<uint4*>(slot_of(t, il, jj));
-          const uint4 v = *dst;
-          const uint32_t rr[4] = {v.x, v.y, v.z, v.w};
-          float f[8];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            f[2 * e2] = __uint_as_float(rr[e2] << 16) * down;
-            f[2 * e2 + 1] = __uint_as_float(rr[e2] & 0xFFFF0000u) * down;
-          }
-          float g8[8];
-          if (FMT == 2) {   // even class (0,4) (2,6), then odd class (1,5) (3,7)
-            g8[0] = f[0]; g8[1] = f[4]; g8[2] = f[2]; g8[3] = f[6]; g8[4] = f[1]; g8[5] = f[5]; g8[6] = f[3]; g8[7] = f[7];
-          } else {          // byte pairs (0,2) (1,3) of each word
-            g8[0] = f[0]; g8[1] = f[2]; g8[2] = f[1]; g8[3] = f[3]; g8[4] = f[4]; g8[5] = f[6]; g8[6] = f[5]; g8[7] = f[7];
-          }
-          uint32_t o[4];
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            __half2 h = __floats2half2_rn(g8[2 * e2], g8[2 * e2 + 1]);
-            o[e2] = *reinterpret_cast<uint32_t*>(&h);
-          }
-          // the values are exact in fp16, so the class sums use the converted values
-          se = (g8[0] + g8[1]) + (g8[2] + g8[3]);
-          so = (g8[4] + g8[5]) + (g8[6] + g8[7]);
-          if (FMT == 1) { se += so; so = 0.f; }
-          *dst = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        // class sums of a unit: its CPU consecutive lanes, fixed shuffle tree
-#pragma unroll
-        for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) {
-          se += __shfl_xor_sync(0xffffffffu, se, o2);
-          so += __shfl_xor_sync(0xffffffffu, so, o2);
-        }
-        if (valid && (jj % CPU) == 0)
-          corr[t * units_staged + il * RANGE_UNITS + jj / CPU] = (FMT == 2) ? fmaf(1032.f, se, 72.f * so) : 1152.f * se;
       }
-      named_sync(1, CT);
-    }
 
     // ------------------------------------------------------------------ stream, dequantise, multiply
     const int grp = warp / GW;    // group
