@@ -78,24 +78,31 @@ int check_weight_input(const void* w, int dt, int64_t N, int64_t K, int64_t kmul
 }  // namespace
 
 // ------------------------------------------------------------------------------------------- interleave
+// [G][M][Nl] -> [M][G * Nl]: source row (g, m) of Nl values is destination row m, columns [g Nl, (g + 1) Nl).
+// One CTA per row at a time; 16-byte vectors when the rows allow it (HBM-bound copy).
 __global__ void interleave_kernel(const uint16_t* __restrict__ src, int G, int64_t M, int64_t Nl,
-                                  uint16_t* __restrict__ dst) {
-  const int64_t total = static_cast<int64_t>(G) * M * Nl;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t j = i % Nl;
-    const int64_t m = (i / Nl) % M;
-    const int64_t g = i / (Nl * M);
-    dst[m * (Nl * G) + g * Nl + j] = src[i];
+                                  uint16_t* __restrict__ dst, int vec) {
+  const int64_t rows = static_cast<int64_t>(G) * M;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t g = r / M, m = r - g * M;
+    const uint16_t* s = src + r * Nl;
+    uint16_t* d = dst + (m * G + g) * Nl;
+    if (vec) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(s);
+      uint4* d4 = reinterpret_cast<uint4*>(d);
+      for (int64_t j = threadIdx.x; j < Nl / 8; j += blockDim.x) d4[j] = s4[j];
+    } else {
+      for (int64_t j = threadIdx.x; j < Nl; j += blockDim.x) d[j] = s[j];
+    }
   }
 }
 
-cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, cudaStream_t st) {
-  const int64_t total = static_cast<int64_t>(G) * M * Nl;
-  int64_t blocks = (total + 255) / 256;
-  if (blocks > 4096) blocks = 4096;
+cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, int sms, cudaStream_t st) {
+  const int64_t rows = static_cast<int64_t>(G) * M;
+  const int vec = (Nl % 8 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 16 == 0);
+  int64_t blocks = rows < static_cast<int64_t>(sms) * 8 ? rows : static_cast<int64_t>(sms) * 8;
   interleave_kernel<<<static_cast<unsigned>(blocks > 0 ? blocks : 1), 256, 0, st>>>(
-      reinterpret_cast<const uint16_t*>(src), G, M, Nl, reinterpret_cast<uint16_t*>(dst));
+      reinterpret_cast<const uint16_t*>(src), G, M, Nl, reinterpret_cast<uint16_t*>(dst), vec);
   return cudaGetLastError();
 }
 
@@ -274,7 +281,7 @@ int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst,
   DevInfo* d;
   int r = current(&d);
   if (r) return r;
-  return launched(launch_interleave(src, G, M, Nl, dst, static_cast<cudaStream_t>(stream)), "interleave");
+  return launched(launch_interleave(src, G, M, Nl, dst, d->sms, static_cast<cudaStream_t>(stream)), "interleave");
 }
 
 }  // extern "C"

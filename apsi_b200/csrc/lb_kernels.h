@@ -27,6 +27,6 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
                         cudaStream_t st, const char** why);
 
-cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, cudaStream_t st);
+cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, int sms, cudaStream_t st);
 
 }  // namespace lb

@@ -17,7 +17,9 @@ all-gather plus one interleave kernel, inside the timed region; the all-gather i
 
 Also reported: the GEMV's live roofline (CUDA events on the launching stream), ``e2e`` through the public API
 (``apsi_b200.precision.qmatmul``) from pinned host memory and back, the reference CPU path (the oracle port of
-``precision.qmatmul``) as ``cpu_baseline``, and the prefill GEMM of configs[2] (M=2048, N=12288, K=4096).
+``precision.qmatmul``) as ``cpu_baseline``, the prefill GEMM of configs[2] (M=2048, N=12288, K=4096), and
+``mlp70b``: the 70B-shaped MLP of configs[4] column-sharded over all ranks (strong scaling) at M = 1, 64 and
+2048, with the per-rank products, the NCCL all-gathers and both together timed separately.
 """
 import argparse
 import json
@@ -36,6 +38,8 @@ METRIC = "int4-g128 W-only GEMV weight GB/s (M=1) & GEMM TFLOP/s (M=2048) vs roo
 M1, N1, K1 = 1, 11008, 4096          # configs[1]
 LAYERS = 128
 GM, GN, GK = 2048, 12288, 4096       # configs[2]
+MLP_N, MLP_K = 28672, 8192           # configs[4]: gate/up [28672, 8192], down [8192, 28672]
+L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM, FALLBACK_TF = 6650.0, 1590.0
 
 
@@ -346,6 +350,9 @@ def run_ours(args, rank, world, local_rank):
     # ---- prefill GEMM, configs[2] (rank 0 reports)
     out["gemm"] = gemm_measure(torch, Kn, FMT_INT4_G128, dev, tf_peak, peak_kind)
 
+    # ---- the 70B-shaped MLP, column-sharded over all ranks (strong scaling)
+    out["mlp70b"] = mlp70b_measure(torch, Kn, FMT_INT4_G128, dev, rank, world, stream, hbm_peak, tf_peak, peak_kind)
+
     if rank == 0 and world == 1:
         try:
             v, dt, cores = cpu_baseline_sample()
@@ -389,6 +396,116 @@ def gemm_measure(torch, Kn, fmt, dev, tf_peak, peak_kind, reps=20):
                          "achieved": round(tf, 1), "peak": tf_peak, "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
                          "peak_source": f"{peak_kind} bf16_tflops (burst)",
                          "traffic": read_traffic("gemm_int4_m2048_12288x4096")}}
+
+
+def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, peak_kind, reps=5):
+    """gate and up [28672, 8192] and down [8192, 28672], int4-g128, each column-sharded over the
+    `world` ranks (rank r holds rows [r N / world, (r + 1) N / world)); strong scaling.  For M in {1, 64, 2048}:
+    the per-rank products of one MLP (three matrices, as a CUDA graph for M = 1), the three NCCL all-gathers
+    plus interleaves on their own, and both together.  Each rank keeps enough distinct weight copies to stream
+    more than twice the L2 per MLP pass, so nothing is served from L2.  Times are the max over ranks."""
+    import torch.distributed as dist
+    shapes = [("gate", MLP_N, MLP_K), ("up", MLP_N, MLP_K), ("down", MLP_K, MLP_N)]
+    per_rank = sum(weight_bytes(n // world, k) for _, n, k in shapes)
+    copies = max(1, -(-2 * L2_BYTES // per_rank))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    mats = []
+    for _ in range(copies):
+        lst = []
+        for _, n, k in shapes:
+            W = torch.randn((n // world, k), generator=gen, device=dev) * 0.015
+            p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+            del W
+            lst.append((p, s16, n // world, k))
+        mats.append(lst)
+    total_w = sum(weight_bytes(n, k) for _, n, k in shapes)
+    flops_per_token = 2 * sum(n * k for _, n, k in shapes)
+
+    def maxed(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    res = {"workload": f"configs[4]: 70B MLP gate/up [{MLP_N},{MLP_K}], down [{MLP_K},{MLP_N}], int4-g128, "
+                       f"column-sharded x{world}" + (" + NCCL all-gather per matrix" if world > 1 else ""),
+           "weight_bytes_per_mlp": total_w, "weight_copies_per_rank": copies, "scaling": "strong"}
+    for M in (1, 64, 2048):
+        xs = {k: torch.randn((M, k), generator=gen, device=dev).to(torch.bfloat16) for k in (MLP_K, MLP_N)}
+        ys = [torch.empty((M, nl), dtype=torch.bfloat16, device=dev) for (_, _, nl, _) in mats[0]]
+        gath = [torch.empty((world, M, nl), dtype=torch.bfloat16, device=dev) for (_, _, nl, _) in mats[0]] \
+            if world > 1 else None
+
+        def compute(c):
+            for j, (p, s16, nl, k) in enumerate(mats[c]):
+                Kn.linear(fmt, xs[k], p, s16, nl, out=ys[j], static_weights=(M <= 16))
+
+        def gather():
+            for j in range(3):
+                dist.all_gather_into_tensor(gath[j].view(-1), ys[j].view(-1))
+                Kn.interleave_cols(gath[j], world, M, ys[j].shape[1])
+
+        with torch.cuda.stream(stream):
+            for c in range(copies):
+                compute(c)
+                if world > 1:
+                    gather()
+        torch.cuda.synchronize(dev)
+        graph = None
+        if M <= 16:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for c in range(copies):
+                    compute(c)
+            torch.cuda.synchronize(dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        if world > 1:
+            dist.barrier()
+        with torch.cuda.stream(stream):
+            ev[0].record(stream)
+            for _ in range(reps):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    for c in range(copies):
+                        compute(c)
+            ev[1].record(stream)
+            if world > 1:
+                ev[2].record(stream)
+                for _ in range(reps * copies):
+                    gather()
+                ev[3].record(stream)
+                ev[4].record(stream)
+                for _ in range(reps):
+                    for c in range(copies):
+                        compute(c)
+                        gather()
+                ev[5].record(stream)
+        torch.cuda.synchronize(dev)
+        n_mlp = reps * copies
+        comp_s = maxed(ev[0].elapsed_time(ev[1]) * 1e-3 / n_mlp)
+        r = {"compute_us_per_mlp": round(comp_s * 1e6, 2)}
+        if M == 1:
+            gbs = total_w / comp_s / 1e9
+            r["weight_GB_per_s"] = round(gbs, 1)
+            r["hbm_frac"] = round(gbs / (hbm_peak * world), 4)
+        else:
+            tf = flops_per_token * M / comp_s / 1e12
+            r["TFLOP_per_s"] = round(tf, 1)
+            r["tensor_frac"] = round(tf / (tf_peak * world), 4)
+        if world > 1:
+            ag_s = maxed(ev[2].elapsed_time(ev[3]) * 1e-3 / n_mlp)
+            e2e_s = maxed(ev[4].elapsed_time(ev[5]) * 1e-3 / n_mlp)
+            recv = sum(M * (n // world) * 2 * (world - 1) for _, n, _ in shapes)
+            r["allgather_us_per_mlp"] = round(ag_s * 1e6, 2)
+            r["allgather_bytes_received_per_rank"] = recv
+            r["allgather_GB_per_s_per_rank"] = round(recv / ag_s / 1e9, 1)
+            r["compute_plus_gather_us_per_mlp"] = round(e2e_s * 1e6, 2)
+        res[f"M={M}"] = r
+        del graph
+    res["peaks"] = f"{peak_kind} hbm_gbs {hbm_peak} and bf16_tflops {tf_peak}, times world size"
+    return res
 
 
 def run_case(case):
