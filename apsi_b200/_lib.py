@@ -14,6 +14,9 @@ LB_E_ARG, LB_E_ALIGN, LB_E_DEVICE, LB_E_LAUNCH, LB_E_WORKSPACE, LB_E_UNSUPPORTED
 FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32 = 1, 2, 3, 4
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 DEVERR_WAIT_TIMEOUT = 1
+DEVERR_PEER_TIMEOUT = 2
+IPC_HANDLE_BYTES = 64
+MAX_RANKS = 8
 LINEAR_STATIC_WEIGHTS = 1
 NOALLOC_SCRATCH_BYTES = 16842752
 
@@ -38,6 +41,13 @@ SIGNATURES = [
     ("lb_linear_ex", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, ctypes.c_uint, _P]),
     ("lb_interleave_cols", _I, [_P, _I, _I64, _I64, _P, _P]),
     ("lb_linear_noalloc", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P]),
+    ("lb_peer_alloc", _I, [_SZ, ctypes.POINTER(_P), _P]),
+    ("lb_peer_open", _I, [_P, ctypes.POINTER(_P)]),
+    ("lb_peer_close", _I, [_P]),
+    ("lb_peer_free", _I, [_P]),
+    ("lb_linear_sharded", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, ctypes.POINTER(_P), _I, _I, _I64, _P, _SZ,
+                               ctypes.c_uint, _P]),
+    ("lb_rank_barrier", _I, [ctypes.POINTER(_P), _I, _I, ctypes.c_uint32, ctypes.c_uint32, _P]),
 ]
 
 

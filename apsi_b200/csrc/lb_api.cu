@@ -232,9 +232,10 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
   return LB_OK;
 }
 
-int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
-                 const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
-                 unsigned flags, void* stream) {
+// Argument checks and dispatch shared by lb_linear_ex and lb_linear_sharded (dst: column-sharded outputs).
+static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+                       const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+                       unsigned flags, void* stream, const OutRanks* dst) {
   if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (flags & ~static_cast<unsigned>(LB_LINEAR_STATIC_WEIGHTS)) return fail(LB_E_ARG, "lb_linear: unknown flags");
@@ -262,11 +263,18 @@ int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & LB_LINEAR_STATIC_WEIGHTS) != 0;
   if (use_gemv(M))
-    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, pdl, st), "gemv");
+    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, pdl, st, dst), "gemv");
   const char* why = nullptr;
-  cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why);
+  cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why, dst);
   if (e != cudaSuccess && why) return fail(LB_E_LAUNCH, "gemm: %s (%s)", why, cudaGetErrorString(e));
   return launched(e, "gemm");
+}
+
+int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
+                 const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
+                 unsigned flags, void* stream) {
+  return linear_impl(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, ws_bytes, flags, stream,
+                     nullptr);
 }
 
 int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,

@@ -44,6 +44,7 @@ struct GemmParams {
   int64_t M, N, K, ldy;
   int acc;
   int m_blocks, n_blocks, tiles, ksteps;
+  OutRanks dst;             // column-sharded layer: every rank's output (dst.n == 0: y)
 };
 
 template <int FMT>
@@ -360,9 +361,15 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           if (row_ok && tok < p.M) {
             float v = __uint_as_float(dv[j]) * (p.tokscale[tok] * rs);
             v += bias;
-            uint16_t* yp = p.y + tok * p.ldy + row;
-            if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
-            *yp = f32_to_bf16_bits_g(v);
+            if (p.dst.n) {                  // this rank's column of every rank's output
+              const uint16_t bb = f32_to_bf16_bits_g(v);
+              const int64_t off = tok * p.ldy + p.dst.col0 + row;
+              for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = bb;
+            } else {
+              uint16_t* yp = p.y + tok * p.ldy + row;
+              if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
+              *yp = f32_to_bf16_bits_g(v);
+            }
           }
         }
       }
@@ -370,6 +377,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
+    if (p.dst.n) __threadfence_system();    // peer stores performed before a later barrier's flag
   }
 
   tc_fence_before();
@@ -430,7 +438,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, c
 
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
-                        cudaStream_t st, const char** why) {
+                        cudaStream_t st, const char** why, const OutRanks* dst) {
   PFN_encodeTiled enc = get_encode();
   if (!enc) {
     *why = "cuTensorMapEncodeTiled is not available from the driver";
@@ -492,6 +500,7 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   p.n_blocks = static_cast<int>((M + BN - 1) / BN);
   p.tiles = p.m_blocks * p.n_blocks;
   p.ksteps = static_cast<int>(K / gemm::BK);
+  p.dst = dst ? *dst : OutRanks{};
   if (fmt == 2) {
     if (BN == 64) return launch_gemm_t<2, 64>(tx, tw, p, sms, st);
     if (BN == 128) return launch_gemm_t<2, 128>(tx, tw, p, sms, st);

@@ -68,6 +68,7 @@ struct GemvParams {
   int C;                  // clusters; cluster c takes row blocks c, c + C, ...
   int slots;              // ring slots
   int max_items;          // item partials per CTA (shared-memory table), 0 = outputs written directly
+  OutRanks dst;           // column-sharded layer: every rank's output (dst.n == 0: y)
 };
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
@@ -202,6 +203,12 @@ template <int FMT>
 __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int tok, float v) {
   if (FMT == 1) v *= __half2float(p.s16[n]);
   if (p.bias) v += bf16_bits_to_f32(p.bias[n]);
+  if (p.dst.n) {                            // this rank's column of every rank's output
+    const uint16_t b = f32_to_bf16_bits(v);
+    const int64_t off = static_cast<int64_t>(tok) * p.ldy + p.dst.col0 + n;
+    for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = b;
+    return;
+  }
   uint16_t* yp = p.y + static_cast<int64_t>(tok) * p.ldy + n;
   if (p.acc) v += bf16_bits_to_f32(*yp);
   *yp = f32_to_bf16_bits(v);
@@ -563,6 +570,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     }
     if (R > 1) asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
+  if (p.dst.n) __threadfence_system();      // peer stores performed before a later barrier's flag
 }
 
 // ------------------------------------------------------------------------------------------- launcher
@@ -638,7 +646,7 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
 
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st) {
+                        cudaStream_t st, const OutRanks* dst) {
   GemvParams p;
   p.x = reinterpret_cast<const uint16_t*>(x);
   p.w = reinterpret_cast<const uint8_t*>(codes);
@@ -653,6 +661,7 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.nblocks = static_cast<int>((N + gemv::RB - 1) / gemv::RB);
   p.nr = (p.total_units + gemv::RANGE_UNITS - 1) / gemv::RANGE_UNITS;
   p.R = 1; p.C = 1; p.slots = 2; p.max_items = 0;
+  p.dst = dst ? *dst : OutRanks{};
   // one token tile: three groups (12 warps + producer) and six ring slots; two token tiles: two groups
   if (fmt == 2)
     return M <= 8 ? launch_gemv_t<2, 1, 3, 1>(p, sms, 1, 6, pdl, st)

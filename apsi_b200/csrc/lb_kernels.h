@@ -6,6 +6,16 @@
 
 namespace lb {
 
+// Where a product's outputs go.  n == 0: the caller's y.  n > 0 (column-sharded layer): every rank's full
+// output y[g] ([M, ldy], the same ldy on every rank), this rank's columns starting at col0; the stores to other
+// ranks' buffers go over NVLink (peer memory opened through CUDA IPC).
+constexpr int kMaxRanks = 8;
+struct OutRanks {
+  uint16_t* y[kMaxRanks];
+  int n;
+  int64_t col0;
+};
+
 cudaError_t launch_quant_int4_g128(const void* w, int dt, int64_t N, int64_t K, uint8_t* packed, uint16_t* s16,
                                    float* s32, int sms, cudaStream_t st);
 cudaError_t launch_quant_int8_rows(const void* w, int dt, int64_t N, int64_t K, int8_t* codes, uint16_t* s16,
@@ -20,12 +30,12 @@ cudaError_t launch_dequant(int fmt, const void* codes, const void* scales, int s
 int gemv_max_k(int fmt);
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st);
+                        cudaStream_t st, const OutRanks* dst = nullptr);
 
 size_t gemm_workspace_bytes(int64_t M, int64_t K);
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
-                        cudaStream_t st, const char** why);
+                        cudaStream_t st, const char** why, const OutRanks* dst = nullptr);
 
 cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, int sms, cudaStream_t st);
 

@@ -4,3 +4,4 @@
 #include "lb_gemm.cu"
 #include "lb_api.cu"
 #include "lb_noalloc.cu"
+#include "lb_peer.cu"

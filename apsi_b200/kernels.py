@@ -202,3 +202,78 @@ def device_errors(device=None):
     with torch.cuda.device(device):
         _lib.call("lb_device_errors", _stream(device), ctypes.byref(v))
     return v.value
+
+
+# ----------------------------------------------------------------------------------------- multi-GPU
+class _DevBuf:
+    """A raw device allocation as torch sees it through the CUDA array interface (torch does not own it)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def peer_alloc(nbytes, device):
+    """A zeroed buffer other processes can map: (uint8 tensor view, device pointer, IPC handle bytes).
+
+    The memory belongs to the library; release it with ``peer_free(ptr, device)`` once no rank uses it."""
+    device = torch.device(device)
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _lib.call("lb_peer_alloc", int(nbytes), ctypes.byref(p), h)
+        t = torch.as_tensor(_DevBuf(p.value, int(nbytes)), device=device)
+    return t, p.value, h.raw
+
+
+def peer_open(handle, device):
+    """Device pointer of another rank's ``peer_alloc`` buffer, mapped into this process."""
+    p = ctypes.c_void_p()
+    with torch.cuda.device(torch.device(device)):
+        _lib.call("lb_peer_open", handle, ctypes.byref(p))
+    return p.value
+
+
+def peer_close(ptr, device):
+    with torch.cuda.device(torch.device(device)):
+        _lib.call("lb_peer_close", ptr)
+
+
+def peer_free(ptr, device):
+    with torch.cuda.device(torch.device(device)):
+        _lib.call("lb_peer_free", ptr)
+
+
+def linear_sharded(fmt, x, codes, scales, n_local, y_ptrs, rank, ldy, bias=None, static_weights=False):
+    """This rank's columns [rank * n_local, (rank + 1) * n_local) of x . deq(W)^T (+ bias), stored into every
+    rank's [M, ldy] output (``y_ptrs``: one device pointer per rank, this rank's own included).  Follow with
+    ``rank_barrier`` before reading an output."""
+    if not (isinstance(x, torch.Tensor) and x.is_cuda):
+        _need_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "x must be a contiguous bfloat16 tensor")
+    K = x.shape[-1]
+    M = x.numel() // K
+    dev = x.device
+    G = len(y_ptrs)
+    arr = (ctypes.c_void_p * G)(*y_ptrs)
+    with torch.cuda.device(dev):
+        nbytes = 0 if M <= 16 else linear_workspace_bytes(fmt, M, n_local, K)
+        ws = _workspace(dev, nbytes) if nbytes else None
+        rc = _fn("lb_linear_sharded")(fmt, x.data_ptr(), M, K, codes.data_ptr(), scales.data_ptr(), n_local,
+                                      bias.data_ptr() if bias is not None else None, arr, G, rank, ldy,
+                                      ws.data_ptr() if ws is not None else None, nbytes,
+                                      _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0,
+                                      torch.cuda.current_stream(dev).cuda_stream)
+    if rc:
+        _lib.check(rc)
+
+
+def rank_barrier(flag_ptrs, rank, epoch, device, timeout_ms=0):
+    """Cross-rank barrier on the current stream (see lb_rank_barrier); ``flag_ptrs``: every rank's flag array."""
+    G = len(flag_ptrs)
+    arr = (ctypes.c_void_p * G)(*flag_ptrs)
+    device = torch.device(device)
+    with torch.cuda.device(device):
+        _lib.call("lb_rank_barrier", arr, G, rank, ctypes.c_uint32(epoch & 0xFFFFFFFF),
+                  ctypes.c_uint32(timeout_ms), _stream(device))

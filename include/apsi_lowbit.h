@@ -58,6 +58,7 @@ extern "C" {
 
 /* device error word bits (lb_device_errors) */
 #define LB_DEVERR_WAIT_TIMEOUT 1 /* a bounded device-side wait (mbarrier) gave up; the output is invalid */
+#define LB_DEVERR_PEER_TIMEOUT 2 /* lb_rank_barrier gave up waiting for another rank; its output is incomplete */
 
 /* ---------------------------------------------------------------------------------------------- runtime */
 
@@ -162,6 +163,38 @@ int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, const void* 
 /* Reassembles column shards after an all-gather: src [G][M][Nl] (rank-major, bf16) -> dst [M][G*Nl].
  * No reference counterpart (the reference has no multi-GPU inference, apsi/hub_gpu.py:1772-1796). */
 int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst, void* stream);
+
+/* Bytes of a CUDA IPC memory handle as lb_peer_alloc writes it. */
+#define LB_IPC_HANDLE_BYTES 64
+/* Maximum ranks of a column-sharded layer. */
+#define LB_MAX_RANKS 8
+
+/* Device memory another process on the same node can map: `bytes` zeroed bytes on the current device, and the
+ * CUDA IPC handle (LB_IPC_HANDLE_BYTES) the caller sends to the other ranks.  Free with lb_peer_free.
+ * No reference counterpart (the reference has no multi-GPU path). */
+int lb_peer_alloc(size_t bytes, void** ptr, void* handle);
+/* Maps another process's lb_peer_alloc buffer into this process (peer access over NVLink); unmap with
+ * lb_peer_close.  A handle from this same process cannot be opened. */
+int lb_peer_open(const void* handle, void** ptr);
+int lb_peer_close(void* ptr);
+int lb_peer_free(void* ptr);
+
+/* The column-sharded product with its gather fused in: this rank holds rows [rank Nl, (rank + 1) Nl) of the
+ * layer's codes and scales (its own lb_quant_* output) and computes y[:, rank Nl + n] for n < Nl, storing each
+ * value into EVERY rank's full output y_ranks[g] ([M, ldy] bf16, ldy >= G Nl; y_ranks is a host array of G
+ * device pointers, the other ranks' buffers opened with lb_peer_open).  Same arithmetic as lb_linear on the
+ * whole layer, so the assembled output is bit-identical to it; bias (bf16 [Nl], this rank's slice) as there;
+ * no accumulate.  Call lb_rank_barrier afterwards before any rank reads its y.  Replaces the N-sharded linear
+ * plus ncclAllGather of the scope's multi-GPU row; no reference counterpart. */
+int lb_linear_sharded(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
+                      int64_t Nl, const void* bias, void* const* y_ranks, int G, int rank, int64_t ldy,
+                      void* workspace, size_t ws_bytes, unsigned flags, void* stream);
+/* Cross-rank barrier on `stream`: makes this rank's earlier stores (its lb_linear_sharded outputs) visible to
+ * every rank, marks this rank's arrival with `epoch` in every rank's flag array and waits until all ranks have
+ * arrived.  flags_ranks: host array of G device pointers, rank g's array of G uint32 (an lb_peer_alloc buffer,
+ * zeroed; the others opened with lb_peer_open).  `epoch` starts at 1 and grows by one per barrier on every rank.
+ * The wait gives up after timeout_ms (0: 2000 ms) and sets LB_DEVERR_PEER_TIMEOUT (read with lb_device_errors). */
+int lb_rank_barrier(uint32_t* const* flags_ranks, int G, int rank, uint32_t epoch, uint32_t timeout_ms, void* stream);
 
 #ifdef __cplusplus
 }

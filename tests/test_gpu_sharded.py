@@ -1,5 +1,7 @@
-"""Column-sharded layer on real GPUs: NCCL ranks, the library's kernels as each rank's product, the gathered
-output bit-identical to the unsharded product.  Needs two or more GPUs (skipped otherwise)."""
+"""Column-sharded layer on real GPUs: NCCL ranks, the library's kernels as each rank's product, the assembled
+output bit-identical to the unsharded product -- through the NCCL all-gather, and with the gather fused into
+the product (peer stores over NVLink + the flag barrier).  The multi-rank tests need two or more GPUs (skipped
+otherwise); the barrier's timeout is tested on one GPU."""
 import os
 import socket
 
@@ -16,7 +18,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, N, K, out_dir):
+def _worker(rank, world, port, M, N, K, out_dir, mode="nccl"):
     import datetime
     import torch.distributed as dist
     from apsi_b200 import sharded, kernels
@@ -33,28 +35,65 @@ def _worker(rank, world, port, M, N, K, out_dir):
         gen.manual_seed(17)                             # the same W and x on every rank
         W = torch.randn((N, K), generator=gen, device=dev) * 0.02
         x = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
-        layer = sharded.ColumnShardedLinear.from_weight(W, FMT_INT4_G128)
-        y = layer(x)
-        torch.cuda.synchronize(dev)
-        if rank == 0:
-            packed, s16, _ = kernels.quant_int4_g128(W, want_scale32=False)
-            full = kernels.linear(FMT_INT4_G128, x, packed, s16, N)
+        peers = sharded.PeerOutputs(N, M, dev) if mode == "p2p" else None
+        layer = sharded.ColumnShardedLinear.from_weight(W, FMT_INT4_G128, peers=peers)
+        outs = []
+        for call in range(3):                           # p2p: both output buffers, then the first again
+            xc = x if call == 0 else torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
+            y = layer(xc)
             torch.cuda.synchronize(dev)
-            np.save(os.path.join(out_dir, "y.npy"), y.view(torch.int16).cpu().numpy())
-            np.save(os.path.join(out_dir, "full.npy"), full.view(torch.int16).cpu().numpy())
+            outs.append((xc, y.clone()))
+        if mode == "p2p":
+            assert kernels.device_errors(dev) == 0
+        packed, s16, _ = kernels.quant_int4_g128(W, want_scale32=False)
+        for call, (xc, y) in enumerate(outs):
+            full = kernels.linear(FMT_INT4_G128, xc, packed, s16, N)
+            torch.cuda.synchronize(dev)
+            np.save(os.path.join(out_dir, f"y{rank}_{call}.npy"), y.view(torch.int16).cpu().numpy())
+            np.save(os.path.join(out_dir, f"full{rank}_{call}.npy"), full.view(torch.int16).cpu().numpy())
+        if peers is not None:
+            peers.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("M,N,K", [(1, 11008, 4096), (4, 4096, 11008), (64, 2048, 4096)])
-def test_nccl_column_shards_match_unsharded_bits(tmp_path, M, N, K):
+def test_column_shards_match_unsharded_bits(tmp_path, M, N, K, mode):
     import torch.multiprocessing as mp
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), M, N, K, str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), M, N, K, str(tmp_path), mode), nprocs=world, join=True,
                        start_method="spawn")
-    y = np.load(tmp_path / "y.npy")
-    full = np.load(tmp_path / "full.npy")
-    assert y.shape == full.shape == (M, N)
-    assert np.array_equal(y, full)
+    for rank in range(world):
+        for call in range(3):
+            y = np.load(tmp_path / f"y{rank}_{call}.npy")
+            full = np.load(tmp_path / f"full{rank}_{call}.npy")
+            assert y.shape == full.shape == (M, N)
+            assert np.array_equal(y, full), (rank, call)
+
+
+def test_rank_barrier_reports_a_rank_that_never_arrives(cuda):
+    """One GPU: a barrier of two ranks where the second never arrives (its flag is never written) gives up
+    after its time limit, reports LB_DEVERR_PEER_TIMEOUT, and the context stays usable."""
+    from apsi_b200 import kernels
+    from apsi_b200._lib import DEVERR_PEER_TIMEOUT, FMT_INT4_G128
+    kernels.device_errors(cuda)                          # start clean
+    mine = torch.zeros(2, dtype=torch.int32, device=cuda)
+    other = torch.zeros(2, dtype=torch.int32, device=cuda)
+    kernels.rank_barrier([mine.data_ptr(), other.data_ptr()], 0, 1, cuda, timeout_ms=50)
+    torch.cuda.synchronize(cuda)
+    assert kernels.device_errors(cuda) == DEVERR_PEER_TIMEOUT
+    assert mine.tolist() == [1, 0] and other.tolist() == [1, 0]   # rank 0 arrived in both arrays
+    # both ranks arrived: no timeout
+    other_side = torch.tensor([1, 1], dtype=torch.int32, device=cuda)
+    kernels.rank_barrier([other_side.data_ptr(), other.data_ptr()], 0, 1, cuda, timeout_ms=50)
+    torch.cuda.synchronize(cuda)
+    assert kernels.device_errors(cuda) == 0
+    W = torch.randn((256, 1024), device=cuda) * 0.02
+    p, s16, _ = kernels.quant_int4_g128(W, want_scale32=False)
+    x = torch.randn((1, 1024), device=cuda).to(torch.bfloat16)
+    y = kernels.linear(FMT_INT4_G128, x, p, s16, 256)
+    torch.cuda.synchronize(cuda)
+    assert torch.isfinite(y.float()).all() and kernels.device_errors(cuda) == 0
