@@ -377,7 +377,6 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
-    if (p.dst.n) __threadfence_system();    // peer stores performed before a later barrier's flag
   }
 
   tc_fence_before();

@@ -570,7 +570,6 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     }
     if (R > 1) asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
-  if (p.dst.n) __threadfence_system();      // peer stores performed before a later barrier's flag
 }
 
 // ------------------------------------------------------------------------------------------- launcher

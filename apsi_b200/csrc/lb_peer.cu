@@ -11,12 +11,15 @@
 // Peer buffers: lb_peer_alloc (cudaMalloc + an IPC handle the caller exchanges between ranks), lb_peer_open /
 // lb_peer_close on the other ranks, lb_peer_free by the owner.
 //
-// Barrier: each rank owns an array of G 32-bit flags in a peer buffer.  lb_rank_barrier(epoch) makes this
-// rank's earlier stores visible system-wide, writes `epoch` into slot `rank` of every rank's array (release
-// store at system scope) and waits until every slot of its own array has reached `epoch` (acquire loads).  The
+// Barrier: each rank owns an array of G 32-bit flags in a peer buffer.  lb_rank_barrier(epoch) runs after the
+// products in stream order; its system-scope fence and release stores order every store of those kernels
+// (local and peer) before the flag it writes into slot `rank` of every rank's array, and it waits until every
+// slot of its own array has reached `epoch` (acquire loads), i.e. every rank's stores are visible here.  The
 // wait gives up after a time limit, sets LB_DEVERR_PEER_TIMEOUT in the device error word and returns, so a
 // rank that never arrives is reported, not waited on for ever.  Epochs increase by one per call on every rank;
 // the comparison is wrap-aware, so a rank that has already reached the next barrier does not stall a slower one.
+// With epoch 0 the barrier takes its epoch from a counter in word G of this rank's own array (incremented on
+// the device), so a captured CUDA graph that replays barriers stays in step on every rank.
 #include <cstring>
 #include "../../include/apsi_lowbit.h"
 #include "lb_common.cuh"
@@ -25,7 +28,7 @@
 namespace lb {
 
 struct BarrierParams {
-  uint32_t* flags[kMaxRanks];   // rank g's flag array (G words), local or IPC-mapped
+  uint32_t* flags[kMaxRanks];   // rank g's flag array (G words + the epoch counter), local or IPC-mapped
   int G, rank;
   uint32_t epoch;
   uint64_t limit_ns;
@@ -42,12 +45,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 __global__ void rank_barrier_kernel(const BarrierParams p) {
   if (threadIdx.x != 0) return;
+  uint32_t* mine = p.flags[p.rank];
+  uint32_t epoch = p.epoch;
+  if (epoch == 0) {                         // device-side counter: only this thread of this rank touches it
+    epoch = mine[p.G] + 1;
+    if (epoch == 0) epoch = 1;
+    mine[p.G] = epoch;
+  }
   __threadfence_system();
-  for (int g = 0; g < p.G; ++g) st_release_sys(p.flags[g] + p.rank, p.epoch);
-  const uint32_t* mine = p.flags[p.rank];
+  for (int g = 0; g < p.G; ++g) st_release_sys(p.flags[g] + p.rank, epoch);
   const uint64_t t0 = global_ns();
   for (int g = 0; g < p.G; ++g) {
-    for (uint32_t i = 0; static_cast<int32_t>(ld_acquire_sys(mine + g) - p.epoch) < 0; ++i) {
+    for (uint32_t i = 0; static_cast<int32_t>(ld_acquire_sys(mine + g) - epoch) < 0; ++i) {
       if (i > (1u << 28) || global_ns() - t0 > p.limit_ns) {
         atomicOr(&g_dev_errors, LB_DEVERR_PEER_TIMEOUT);
         return;

@@ -81,7 +81,7 @@ class PeerOutputs:
             self._views.append(t.view(torch.bfloat16).view(self.max_rows, self.N))
             self._own.append(p)
             handles.append(h)
-        tf, pf, hf = kernels.peer_alloc(4 * self.world, self.device)
+        tf, pf, hf = kernels.peer_alloc(4 * (self.world + 1), self.device)   # G flags + the epoch counter
         self._own.append(pf)
         handles.append(hf)
         everyone = [None] * self.world
@@ -108,9 +108,10 @@ class PeerOutputs:
         return self.ptrs[b], self._views[b][:M]
 
     def finish(self):
-        """Barrier: every rank's stores of this call are visible on every rank (on the current stream)."""
+        """Barrier: every rank's stores of this call are visible on every rank (on the current stream).  The
+        barrier's epoch comes from the device-side counter, so the call may be captured in a CUDA graph."""
         self.epoch += 1
-        kernels.rank_barrier(self.ptrs[2], self.rank, self.epoch, self.device, self.timeout_ms)
+        kernels.rank_barrier(self.ptrs[2], self.rank, 0, self.device, self.timeout_ms)
 
     def close(self):
         torch.cuda.synchronize(self.device)

@@ -12,8 +12,9 @@ every GEMV streams its weights from HBM (inputs are larger than L2; nothing is f
 CUDA-graph replay of 128 GEMV launches.  ``value`` is packed weight bytes per second over all ranks.
 
 N > 1 (torchrun): each rank holds the column shards of 128 layers that are N times as wide (weak scaling:
-[11008, 4096] per rank per layer); after the GEMVs the N-sharded outputs are reassembled with an NCCL
-all-gather plus one interleave kernel, inside the timed region; the all-gather is also timed on its own.
+[11008, 4096] per rank per layer).  The gather is fused into the GEMVs: every rank's GEMV stores its columns
+into every rank's full output over NVLink (CUDA IPC peer buffers), and one flag barrier ends the step, all
+inside the timed CUDA graph.  An NCCL all-gather of the same outputs is timed on its own for comparison.
 
 Also reported: the GEMV's live roofline (CUDA events on the launching stream), ``e2e`` through the public API
 (``apsi_b200.precision.qmatmul``) from pinned host memory and back, the reference CPU path (the oracle port of
@@ -197,6 +198,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     from apsi_b200 import kernels as Kn
     from apsi_b200 import precision as P
+    from apsi_b200 import sharded as S
     from apsi_b200._lib import FMT_INT4_G128
 
     dev = torch.device("cuda", local_rank)
@@ -216,10 +218,19 @@ def run_ours(args, rank, world, local_rank):
     x = torch.randn((M1, K1), generator=gen, device=dev).to(torch.bfloat16)
     ys = torch.empty((LAYERS, M1, N1), dtype=torch.bfloat16, device=dev)
     gathered = torch.empty((world, LAYERS * M1, N1), dtype=torch.bfloat16, device=dev) if world > 1 else None
+    # N > 1: every rank's full outputs [LAYERS * M1, N1 * world], written by all ranks' GEMVs (fused gather)
+    peers = S.PeerOutputs(N1 * world, LAYERS * M1, dev) if world > 1 else None
 
     def sweep():
+        if peers is None:
+            for i in range(LAYERS):
+                Kn.linear(FMT_INT4_G128, x, packed[i], scales[i], N1, out=ys[i], static_weights=True)
+            return
+        ldy = N1 * world
         for i in range(LAYERS):
-            Kn.linear(FMT_INT4_G128, x, packed[i], scales[i], N1, out=ys[i], static_weights=True)
+            ptrs = [q + i * M1 * ldy * 2 for q in peers.ptrs[0]]
+            Kn.linear_sharded(FMT_INT4_G128, x, packed[i], scales[i], N1, ptrs, rank, ldy, static_weights=True)
+        Kn.rank_barrier(peers.ptrs[2], rank, 0, dev)       # epoch from the device counter: graph-safe
 
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
@@ -241,9 +252,6 @@ def run_ours(args, rank, world, local_rank):
             graph.replay()
             if i is not None:
                 ev_b[i].record(stream)
-            if world > 1:
-                dist.all_gather_into_tensor(gathered.view(-1), ys.view(-1))
-                Kn.interleave_cols(gathered, world, LAYERS * M1, N1)
 
     for _ in range(args.warmup):
         step()
@@ -286,18 +294,19 @@ def run_ours(args, rank, world, local_rank):
                                   f"{LAYERS} distinct resident weight matrices per step",
                       "M": M1, "N": N1 * world, "N_per_rank": N1, "K": K1, "layers_per_step": LAYERS,
                       "weight_bytes_per_step": wb_step, "l2": "inputs larger than L2 (no flush)",
-                      "parallelism": f"column-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                      "parallelism": f"column-shard x{world}" + (" + gather fused into the GEMVs (peer stores over "
+                                                                 "NVLink) + flag barrier" if world > 1 else ""),
                       "graph": "one CUDA graph replay of the GEMV launches per step"},
            "roofline": {"kernel": "gemv_kernel<int4,1>", "bound": "hbm", "achieved": round(achieved, 1),
                         "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                         "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs",
                         "algorithmic_bytes_per_launch": gemv_bytes(M1, N1, K1),
                         "avg_launch_us": round(launch_s * 1e6, 3)},
-           "gpu_launches": args.steps * LAYERS + (args.steps if world > 1 else 0),
+           "gpu_launches": args.steps * (LAYERS + (1 if world > 1 else 0)),
            "device_error_bits": errs}
     out["clocks"] = clk.summary(w0, w1)
 
-    # ---- all-gather alone (N > 1)
+    # ---- NCCL all-gather of the same outputs, alone (N > 1; the unfused alternative)
     if world > 1:
         torch.cuda.synchronize(dev)
         dist.barrier()
@@ -312,7 +321,8 @@ def run_ours(args, rank, world, local_rank):
         ag = torch.tensor([a0.elapsed_time(a1) / reps], dtype=torch.float64, device=dev)
         dist.all_reduce(ag, op=dist.ReduceOp.MAX)
         per_rank = ys.numel() * 2 * (world - 1)
-        out["allgather"] = {"ms": round(float(ag), 4), "bytes_received_per_rank": per_rank,
+        out["allgather"] = {"what": "NCCL all_gather_into_tensor of one step's outputs (not on the timed path)",
+                            "ms": round(float(ag), 4), "bytes_received_per_rank": per_rank,
                             "GB_per_s_per_rank": round(per_rank / (float(ag) * 1e-3) / 1e9, 2)}
 
     # ---- e2e through the public API: pinned host x in, every layer's y back to pinned host memory
@@ -363,6 +373,8 @@ def run_ours(args, rank, world, local_rank):
             out["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
                                    "sample": f"failed: {type(e).__name__}: {e}"}
     del graph
+    if peers is not None:
+        peers.close()
     if rank == 0:
         print(json.dumps(out), flush=True)
     return 0
@@ -401,10 +413,13 @@ def gemm_measure(torch, Kn, fmt, dev, tf_peak, peak_kind, reps=20):
 def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, peak_kind, reps=5):
     """gate and up [28672, 8192] and down [8192, 28672], int4-g128, each column-sharded over the
     `world` ranks (rank r holds rows [r N / world, (r + 1) N / world)); strong scaling.  For M in {1, 64, 2048}:
-    the per-rank products of one MLP (three matrices, as a CUDA graph for M = 1), the three NCCL all-gathers
-    plus interleaves on their own, and both together.  Each rank keeps enough distinct weight copies to stream
-    more than twice the L2 per MLP pass, so nothing is served from L2.  Times are the max over ranks."""
+    the per-rank products of one MLP (three matrices, as a CUDA graph for M = 1); with several ranks also the
+    three NCCL all-gathers plus interleaves on their own, products and all-gathers together, and the products
+    with the gather fused in (peer stores over NVLink + one flag barrier per matrix).  Each rank keeps enough
+    distinct weight copies to stream more than twice the L2 per MLP pass, so nothing is served from L2.  Times
+    are the max over ranks."""
     import torch.distributed as dist
+    from apsi_b200 import sharded as S
     shapes = [("gate", MLP_N, MLP_K), ("up", MLP_N, MLP_K), ("down", MLP_K, MLP_N)]
     per_rank = sum(weight_bytes(n // world, k) for _, n, k in shapes)
     copies = max(1, -(-2 * L2_BYTES // per_rank))
@@ -428,8 +443,10 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t)
 
+    peers = [S.PeerOutputs(n, 2048, dev) for _, n, _ in shapes] if world > 1 else None
     res = {"workload": f"configs[4]: 70B MLP gate/up [{MLP_N},{MLP_K}], down [{MLP_K},{MLP_N}], int4-g128, "
-                       f"column-sharded x{world}" + (" + NCCL all-gather per matrix" if world > 1 else ""),
+                       f"column-sharded x{world}" + (" (gather fused into the products, or NCCL all-gather + "
+                                                    "interleave)" if world > 1 else ""),
            "weight_bytes_per_mlp": total_w, "weight_copies_per_rank": copies, "scaling": "strong"}
     for M in (1, 64, 2048):
         xs = {k: torch.randn((M, k), generator=gen, device=dev).to(torch.bfloat16) for k in (MLP_K, MLP_N)}
@@ -446,20 +463,32 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                 dist.all_gather_into_tensor(gath[j].view(-1), ys[j].view(-1))
                 Kn.interleave_cols(gath[j], world, M, ys[j].shape[1])
 
+        def fused(c):
+            for j, (p, s16, nl, k) in enumerate(mats[c]):
+                Kn.linear_sharded(fmt, xs[k], p, s16, nl, peers[j].ptrs[0], rank, peers[j].N,
+                                  static_weights=(M <= 16))
+                Kn.rank_barrier(peers[j].ptrs[2], rank, 0, dev)
+
         with torch.cuda.stream(stream):
             for c in range(copies):
                 compute(c)
                 if world > 1:
                     gather()
+                    fused(c)
         torch.cuda.synchronize(dev)
-        graph = None
+        graph = fgraph = None
         if M <= 16:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 for c in range(copies):
                     compute(c)
+            if world > 1:
+                fgraph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(fgraph, stream=stream):
+                    for c in range(copies):
+                        fused(c)
             torch.cuda.synchronize(dev)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
         if world > 1:
             dist.barrier()
         with torch.cuda.stream(stream):
@@ -482,6 +511,14 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                         compute(c)
                         gather()
                 ev[5].record(stream)
+                ev[6].record(stream)
+                for _ in range(reps):
+                    if fgraph is not None:
+                        fgraph.replay()
+                    else:
+                        for c in range(copies):
+                            fused(c)
+                ev[7].record(stream)
         torch.cuda.synchronize(dev)
         n_mlp = reps * copies
         comp_s = maxed(ev[0].elapsed_time(ev[1]) * 1e-3 / n_mlp)
@@ -502,9 +539,18 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
             r["allgather_bytes_received_per_rank"] = recv
             r["allgather_GB_per_s_per_rank"] = round(recv / ag_s / 1e9, 1)
             r["compute_plus_gather_us_per_mlp"] = round(e2e_s * 1e6, 2)
+            fu_s = maxed(ev[6].elapsed_time(ev[7]) * 1e-3 / n_mlp)
+            r["fused_gather_us_per_mlp"] = round(fu_s * 1e6, 2)
+            if M == 1:
+                r["fused_weight_GB_per_s"] = round(total_w / fu_s / 1e9, 1)
+            else:
+                r["fused_TFLOP_per_s"] = round(flops_per_token * M / fu_s / 1e12, 1)
         res[f"M={M}"] = r
-        del graph
+        del graph, fgraph
     res["peaks"] = f"{peak_kind} hbm_gbs {hbm_peak} and bf16_tflops {tf_peak}, times world size"
+    if peers is not None:
+        for q in peers:
+            q.close()
     return res
 
 

@@ -192,8 +192,10 @@ int lb_linear_sharded(int fmt, const void* x, int64_t M, int64_t K, const void* 
 /* Cross-rank barrier on `stream`: makes this rank's earlier stores (its lb_linear_sharded outputs) visible to
  * every rank, marks this rank's arrival with `epoch` in every rank's flag array and waits until all ranks have
  * arrived.  flags_ranks: host array of G device pointers, rank g's array of G uint32 (an lb_peer_alloc buffer,
- * zeroed; the others opened with lb_peer_open).  `epoch` starts at 1 and grows by one per barrier on every rank.
- * The wait gives up after timeout_ms (0: 2000 ms) and sets LB_DEVERR_PEER_TIMEOUT (read with lb_device_errors). */
+ * zeroed; the others opened with lb_peer_open).  `epoch` starts at 1 and grows by one per barrier on every rank;
+ * epoch 0 takes the next epoch from a counter in word G of this rank's array (arrays of G + 1 words), which keeps
+ * barriers captured in a CUDA graph in step across replays.  The wait gives up after timeout_ms (0: 2000 ms) and
+ * sets LB_DEVERR_PEER_TIMEOUT (read with lb_device_errors). */
 int lb_rank_barrier(uint32_t* const* flags_ranks, int G, int rank, uint32_t epoch, uint32_t timeout_ms, void* stream);
 
 #ifdef __cplusplus
