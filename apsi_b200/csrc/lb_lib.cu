@@ -5,3 +5,4 @@
 #include "lb_api.cu"
 #include "lb_noalloc.cu"
 #include "lb_peer.cu"
+#include "lb_norm.cu"

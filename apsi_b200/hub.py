@@ -9,9 +9,11 @@ its kernels:
   ``qmatrix(w, "int8")`` -- int8, one fp16 scale per row.  ``w`` is ``[rows, cols]`` = ``[out, in]``
   (float32, or uint16 bfloat16 bits, as the reference takes it).  Quantised on the device, bit-exact with
   ``precision.quantize``.  The reference's g32 ggml formats and minifloats are not products here and raise.
-* ``linear(m, X, Y, T, bias=None, acc=False, xoff=0)`` -- ``Y (+)= X @ W.T (+ bias)`` for T rows: the decode
-  GEMV for T <= 16, the tcgen05 GEMM above.  ``ln`` (a fused RMSNorm prologue) is not on this path and
-  raises.
+* ``linear(m, X, Y, T, bias=None, acc=False, ln=None, eps=1e-6, off=0.0, xoff=0)`` -- ``Y (+)= norm(X) @ W.T
+  (+ bias)`` for T rows: the decode GEMV for T <= 16, the tcgen05 GEMM above.  With ``ln`` (RMSNorm weights)
+  the rows are first normalised by ``lb_rmsnorm`` into a workspace (``x / sqrt(mean(x^2) + eps) * (ln + off)``,
+  float32 arithmetic, rounded once to bf16), as the reference's GEMM path does with its ``rms`` op.
+* ``rms(X, Y, W, rows, n, eps, off, xoff=0, yoff=0)`` -- that normalisation on its own.
 * ``gemv``, ``gemm``, ``matmul``, ``matmul_rows`` -- the same product under the reference's other names.
 
 One difference in representation: a ``Buf`` here holds bfloat16 elements in a CUDA tensor.  The reference
@@ -144,10 +146,20 @@ class Ops:
         return Matrix(codes, rows, cols, k, s16, fmt)
 
     # ---- products
+    def rms(self, X, Y, W, rows, n, eps, off, xoff=0, yoff=0):
+        """Y[yoff:] = X[xoff:] / sqrt(mean(X^2) + eps) * (W + off) for `rows` rows of n (hub_gpu rms)."""
+        if X.n < xoff + rows * n or Y.n < yoff + rows * n or W.n < n:
+            raise LowbitError(LB_E_ARG, "rms: buffers too small")
+        _k.rmsnorm(X.t[xoff:xoff + rows * n].view(rows, n), W.t[:n], eps=eps, off=off,
+                   out=Y.t[yoff:yoff + rows * n].view(rows, n))
+
     def linear(self, m, X, Y, T, bias=None, acc=False, ln=None, eps=1e-6, off=0.0, xoff=0):
-        """Y (+)= X @ W.T (+ bias) for T rows (X: [T, cols] from element xoff, Y: [T, rows])."""
+        """Y (+)= norm(X) @ W.T (+ bias) for T rows (X: [T, cols] from element xoff, Y: [T, rows]); ln: RMSNorm
+        weights applied to each row of X first."""
         if ln is not None:
-            raise LowbitError(LB_E_UNSUPPORTED, "a fused RMSNorm prologue is not on the B200 low-bit path")
+            Z = self.ws("lnx", T * m.cols)
+            self.rms(X, Z, ln, T, m.cols, eps, off, xoff=xoff)
+            X, xoff = Z, 0
         if X.n < xoff + T * m.cols or Y.n < T * m.rows:
             raise LowbitError(LB_E_ARG, "linear: buffers too small for T rows")
         x = X.t[xoff:xoff + T * m.cols].view(T, m.cols)

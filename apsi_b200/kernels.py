@@ -277,3 +277,25 @@ def rank_barrier(flag_ptrs, rank, epoch, device, timeout_ms=0):
     with torch.cuda.device(device):
         _lib.call("lb_rank_barrier", arr, G, rank, ctypes.c_uint32(epoch & 0xFFFFFFFF),
                   ctypes.c_uint32(timeout_ms), _stream(device))
+
+
+def rmsnorm(x, w, eps=1e-6, off=0.0, out=None):
+    """bf16(x * (1 / sqrt(mean(x^2) + eps)) * (w + off)) per row of bf16 x [.., K]; w float32 or bf16 [K]."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "x must be a contiguous bfloat16 tensor")
+    K = x.shape[-1]
+    M = x.numel() // K
+    w = w.to(x.device)
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    w = w.contiguous()
+    if w.numel() < K:
+        raise LowbitError(_lib.LB_E_ARG, f"w holds {w.numel()} values, K is {K}")
+    if out is None:
+        out = torch.empty_like(x)
+    wdt = _lib.DT_F32 if w.dtype == torch.float32 else _lib.DT_BF16
+    with torch.cuda.device(x.device):
+        _lib.call("lb_rmsnorm", _ptr(x), M, K, _ptr(w), wdt, ctypes.c_float(eps), ctypes.c_float(off), _ptr(out),
+                  _stream(x.device))
+    return out

@@ -116,6 +116,15 @@ int lb_round_g32(int fmt, const void* w, int w_dtype, int64_t N, int64_t K, floa
 int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, int64_t N, int64_t K, void* out,
                int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- norm */
+
+/* RMSNorm of activation rows, the prologue of a normalised projection: out[m, k] = bf16(x[m, k] *
+ * (1 / sqrt(mean_k x[m, :]^2 + eps)) * (w[k] + off)), float32 arithmetic.  x, out: bf16 [M, K] (may alias);
+ * w: [K] in w_dtype (LB_DT_F32 or LB_DT_BF16).  Replaces hub_gpu's rms op and the norm prologue of the
+ * gemvq*n kernels behind _Base.linear(ln=...) (apsi/hub_gpu.py:1690-1693, 837-870, 1305-1315). */
+int lb_rmsnorm(const void* x, int64_t M, int64_t K, const void* w, int w_dtype, float eps, float off, void* out,
+               void* stream);
+
 /* ---------------------------------------------------------------------------------------------- products */
 
 /* Bytes of device workspace lb_linear needs for this shape (0 when none).  Replaces the scratch buffers of

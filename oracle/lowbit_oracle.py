@@ -136,6 +136,14 @@ def linear_ref(x, Wd, bias=None, y0=None):
     return y
 
 
+def rms_norm(x, w, eps=1e-6, off=0.0):
+    """RMSNorm of rows in float32, as the reference's host rms op computes it (apsi/hub_gpu.py:1690-1693):
+    x / sqrt(mean(x * x) + eps) * (w + off)."""
+    x = np.asarray(x, np.float32)
+    w = np.asarray(w, np.float32)
+    return (x / np.sqrt((x * x).mean(-1, keepdims=True) + np.float32(eps)) * (w + np.float32(off))).astype(np.float32)
+
+
 def qmatmul_dequant_reference(x, packed_or_codes, scale16, fmt):
     """The reference CPU path for a quantized product (precision.qmatmul: dequantise, then a float32
     matmul, precision.py:294-299).  This is what ``bench.py --impl reference`` times."""

@@ -6,7 +6,8 @@ Run in a container where the reference is importable (its ``apsi`` package on ``
     python tests/golden/make_golden.py
 
 The outputs come from the reference's own functions -- ``apsi.precision.quantize`` / ``dequantize`` /
-``qmatmul`` and ``apsi.hub_gpu.qnumpy`` -- on seeded inputs, including adversarial ones (exact half-way ties,
+``qmatmul``, ``apsi.hub_gpu.qnumpy``, ``apsi.lowbit.round_weights`` and, for ``ref_packed.apsim``,
+``apsi.modelio.save_model`` -- on seeded inputs, including adversarial ones (exact half-way ties,
 near-ties one ulp either side, all-zero groups, signed zeros, subnormals, single outliers).  The arrays are
 small so the fixture stays a few hundred KB.
 """
@@ -117,6 +118,21 @@ def main():
     out["rw_in"] = Wr
     for kind in ("int8", "int4"):
         out[f"rw_{kind}"] = np.asarray(lowbit.round_weights(Wr, kind), np.float32)
+
+    # ---- a checkpoint written by the reference's own save_model (apsi/modelio.py:417-463): an int4
+    # group-128 layer stored the reference's way (W.reshape(-1, 128), axis 0), an int8 per-row layer, a bias
+    # and a norm vector.  The source arrays go into the npz so the loaded codes can be checked bit for bit.
+    from apsi import modelio  # noqa: E402
+    w4 = (rng.standard_normal((48, 384)) * 0.02).astype(np.float32)
+    w8 = (rng.standard_normal((40, 256)) * 0.02).astype(np.float32)
+    b4 = (rng.standard_normal(48) * 0.1).astype(np.float32)
+    nv = np.ones(384, np.float32)
+    out["apsim_w4"], out["apsim_w8"], out["apsim_b4"], out["apsim_norm"] = w4, w8, b4, nv
+    tree = {"proj": {"W": precision.quantize(w4.reshape(-1, 128), "int4", axis=0), "b": b4},
+            "down": {"W": precision.quantize(w8, "int8", axis=0)}, "norm": nv}
+    apsim = os.path.join(HERE, "ref_packed.apsim")
+    modelio.save_model(apsim, tree, metadata={"written_by": "apsi.modelio.save_model"})
+    print("wrote", apsim)
 
     path = os.path.join(HERE, "lowbit_golden.npz")
     np.savez_compressed(path, **out)

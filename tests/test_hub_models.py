@@ -1,7 +1,8 @@
 """The hub_gpu-style ops object (apsi_b200.hub) and the models entry points (apsi_b200.models).
 
 CPU tests: names, runner() without a GPU, unsupported formats.  GPU tests: qmatrix codes bit-exact with the
-oracle, linear / gemv / gemm / matmul and qlinear within the layer's tolerance of the oracle product."""
+oracle, linear / gemv / gemm / matmul and qlinear within the layer's tolerance of the oracle product, and the
+RMSNorm prologue (linear(ln=...), rms) against the oracle's float32 RMSNorm."""
 import numpy as np
 import pytest
 
@@ -88,3 +89,30 @@ def test_qlinear_on_a_quantized_model(cuda, dtype, M):
     assert yd.is_cuda and _close(yd.float().cpu().numpy(), ref)
     back = models.dequantize_model(q)
     assert back["proj"]["W"].shape == (K, N)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 3, 40])
+def test_ops_linear_with_rmsnorm_prologue(cuda, T):
+    """linear(ln=...) normalises each row first (hub_gpu.py:1305-1315): the result equals the product of the
+    bf16-rounded RMSNorm (oracle, hub_gpu.py:1690-1693) within the layer's tolerance, and rms() alone is
+    within one bf16 rounding of the float32 oracle."""
+    rows, cols = 384, 1024
+    x, W = ora.make_config_inputs(T, rows, cols, seed=5 + T)
+    g = np.random.default_rng(3).standard_normal(cols).astype(np.float32) * 0.1 + 1.0
+    ops = hub.Ops(0)
+    m = ops.qmatrix(W, "int4")
+    packed, _, s16 = ora.quant_int4_g128(W)
+    Wd = ora.dequant_int4_g128(packed, s16)
+    X, LN = ops.vec(x), ops.vec(g)
+    Y = ops.alloc(T * rows)
+    ops.linear(m, X, Y, T, ln=LN, eps=1e-5, off=0.0)
+    xb = ora.bf16_round(x)
+    xn = ora.bf16_round(ora.rms_norm(xb, ora.bf16_round(g), eps=1e-5))
+    assert _close(ops.get(Y, T * rows).reshape(T, rows), ora.linear_ref(xn, Wd))
+    Z = ops.alloc(T * cols)
+    ops.rms(X, Z, LN, T, cols, 1e-5, 0.5)
+    z = ops.get(Z, T * cols).reshape(T, cols)
+    ref = ora.rms_norm(xb, ora.bf16_round(g), eps=1e-5, off=0.5)
+    assert np.all(np.abs(z - ref) <= np.abs(ref) * 2.0 ** -8 + 1e-30)
+    ops.close()
