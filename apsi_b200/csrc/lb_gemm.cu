@@ -176,7 +176,9 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
-template <int FMT, int BN>
+// SH: column-sharded outputs (stores into every rank's buffer); a separate instance, so the ordinary
+// epilogue carries no extra code
+template <int FMT, int BN, bool SH>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                 const GemmParams p) {
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           if (row_ok && tok < p.M) {
             float v = __uint_as_float(dv[j]) * (p.tokscale[tok] * rs);
             v += bias;
-            if (p.dst.n) {                  // this rank's column of every rank's output
+            if constexpr (SH) {             // this rank's column of every rank's output
               const uint16_t bb = f32_to_bf16_bits_g(v);
               const int64_t off = tok * p.ldy + p.dst.col0 + row;
               for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = bb;
@@ -417,7 +419,7 @@ size_t gemm_workspace_bytes(int64_t M, int64_t K) {
   return x16 + static_cast<size_t>(M) * sizeof(float) + 256;
 }
 
-template <int FMT, int BN>
+template <int FMT, int BN, bool SH>
 static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int sms,
                                  cudaStream_t st) {
   const size_t smem = gemm_smem_bytes(FMT, BN);
@@ -425,13 +427,13 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, c
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, BN, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   const int grid = p.tiles < sms ? p.tiles : sms;
-  gemm_kernel<FMT, BN><<<grid, gemm::THREADS, smem, st>>>(tx, tw, p);
+  gemm_kernel<FMT, BN, SH><<<grid, gemm::THREADS, smem, st>>>(tx, tw, p);
   return cudaGetLastError();
 }
 
@@ -501,13 +503,23 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   p.ksteps = static_cast<int>(K / gemm::BK);
   p.dst = dst ? *dst : OutRanks{};
   if (fmt == 2) {
-    if (BN == 64) return launch_gemm_t<2, 64>(tx, tw, p, sms, st);
-    if (BN == 128) return launch_gemm_t<2, 128>(tx, tw, p, sms, st);
-    return launch_gemm_t<2, 256>(tx, tw, p, sms, st);
+    if (p.dst.n) {
+      if (BN == 64) return launch_gemm_t<2, 64, true>(tx, tw, p, sms, st);
+      if (BN == 128) return launch_gemm_t<2, 128, true>(tx, tw, p, sms, st);
+      return launch_gemm_t<2, 256, true>(tx, tw, p, sms, st);
+    }
+    if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, p, sms, st);
+    if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, p, sms, st);
+    return launch_gemm_t<2, 256, false>(tx, tw, p, sms, st);
   }
-  if (BN == 64) return launch_gemm_t<1, 64>(tx, tw, p, sms, st);
-  if (BN == 128) return launch_gemm_t<1, 128>(tx, tw, p, sms, st);
-  return launch_gemm_t<1, 256>(tx, tw, p, sms, st);
+  if (p.dst.n) {
+    if (BN == 64) return launch_gemm_t<1, 64, true>(tx, tw, p, sms, st);
+    if (BN == 128) return launch_gemm_t<1, 128, true>(tx, tw, p, sms, st);
+    return launch_gemm_t<1, 256, true>(tx, tw, p, sms, st);
+  }
+  if (BN == 64) return launch_gemm_t<1, 64, false>(tx, tw, p, sms, st);
+  if (BN == 128) return launch_gemm_t<1, 128, false>(tx, tw, p, sms, st);
+  return launch_gemm_t<1, 256, false>(tx, tw, p, sms, st);
 }
 
 }  // namespace lb

@@ -206,7 +206,9 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int to
   if (p.dst.n) {                            // this rank's column of every rank's output
     const uint16_t b = f32_to_bf16_bits(v);
     const int64_t off = static_cast<int64_t>(tok) * p.ldy + p.dst.col0 + n;
-    for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = b;
+#pragma unroll
+    for (int g = 0; g < kMaxRanks; ++g)     // constant indices: no dynamic indexing of the parameters
+      if (g < p.dst.n) p.dst.y[g][off] = b;
     return;
   }
   uint16_t* yp = p.y + static_cast<int64_t>(tok) * p.ldy + n;
