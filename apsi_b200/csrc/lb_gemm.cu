@@ -29,11 +29,19 @@ namespace lb {
 namespace gemm {
 constexpr int BM = 128;     // weight rows per tile = TMEM lanes
 constexpr int BK = 64;      // K values per stage (128 bytes of fp16: one SW128 row)
-constexpr int STAGES = 4;
 constexpr int DQ_WARPS = 8;
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = (2 + DQ_WARPS + EPI_WARPS) * 32;   // TMA, MMA, dequantisers, epilogue
 constexpr int A_STAGE = BM * BK * 2;                       // 16 KB of fp16 weights per stage
+constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int TAIL = 512;                                  // mbarriers, TMEM address, abort flag
+// Pipeline depth: as many stages as shared memory holds (at most 8).  Narrow token tiles (small M) carry few
+// weight bytes per stage, so they need the deepest pipelines to keep enough of the weight stream in flight.
+__host__ __device__ constexpr int stages(int fmt, int bn) {
+  const int stage = bn * 128 + A_STAGE + BM * ((fmt == 2) ? 32 : 64);
+  const int n = (SMEM_LIMIT - 1024 - TAIL) / stage;
+  return n > 8 ? 8 : n;
+}
 }  // namespace gemm
 
 struct GemmParams {
@@ -185,6 +193,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   using namespace gemm;
   using Cfg = GemmCfg<FMT>;
   using Sm = GemmSmem<BN>;
+  constexpr int STAGES = stages(FMT, BN);
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
   // 1024-align the carve-out (SW128 atoms)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
@@ -410,7 +419,7 @@ static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256)
 
 size_t gemm_smem_bytes(int fmt, int bn) {
   const int raw = (fmt == 2) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
-  return 1024 + static_cast<size_t>(gemm::STAGES) * (bn * 128 + gemm::A_STAGE + raw) + 256;
+  return 1024 + static_cast<size_t>(gemm::stages(fmt, bn)) * (bn * 128 + gemm::A_STAGE + raw) + gemm::TAIL;
 }
 
 size_t gemm_workspace_bytes(int64_t M, int64_t K) {
