@@ -1,0 +1,233 @@
+"""A quantized decoder whose every projection runs on this library's kernels.
+
+It follows the layer sequence of the reference's GPU decoder (``hub_models.Decoder._forward_gpu``,
+apsi/hub_models.py:1018-1092), one block per layer:
+
+    QKV  = linear(qkv, X, ln=ln1)            fused [(nh + 2 kvh) dh, H] projection after RMSNorm
+    q, k, v = split(QKV); rope(q, k); write k, v into the cache        (qkv_prep)
+    O    = attention(q, cache)                                           (attention)
+    X   += linear(o, O)                                                  (o projection, residual add)
+    GU   = linear(gu, X, ln=ln2)             fused [2 I, H] gate/up projection after RMSNorm
+    X   += linear(down, silu(G) * U)                                     (act_mul, down projection)
+    logits = linear(head, X_last, ln=final_norm)
+
+All projections -- QKV, O, gate/up, down and the LM head -- are int4 group-128 (or int8 per-row) weights in
+the library's packed layout, multiplied by ``kernels.linear``: the decode GEMV for up to 16 rows, the tcgen05
+GEMM above; the residual adds are the kernels' accumulate epilogue and the norms ``lb_rmsnorm``.  Embedding
+lookup, rotary position embedding, attention over the KV cache and the SwiGLU product are torch operations:
+they are not on the quantized-linear path this library rebuilds.  Activations are bf16; the KV cache is bf16.
+
+Weights are random (seeded, N(0, 0.02) projections, unit norms), as configs[3] specifies; there is no
+checkpoint.  ``generate`` prefills a batch of prompts and then decodes greedily, one CUDA-graph replay per
+step (static shapes: attention over the whole cache capacity with a position mask).
+"""
+import math
+import time
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as Kn
+from ._lib import FMT_INT4_G128, FMT_INT8_ROW, LowbitError, LB_E_ARG
+
+__all__ = ["DecoderConfig", "QuantDecoder", "KVCache"]
+
+
+@dataclass
+class DecoderConfig:
+    """Llama-style shapes; the defaults are configs[3] (a 7B-class decoder)."""
+    H: int = 4096          # hidden size
+    L: int = 32            # layers
+    nh: int = 32           # attention heads
+    kvh: int = 8           # key/value heads
+    dh: int = 128          # head size
+    I: int = 11008         # SwiGLU width
+    V: int = 32000         # vocabulary
+    eps: float = 1e-5
+    theta: float = 10000.0
+    wstd: float = 0.02
+
+
+class KVCache:
+    """Keys and values of every layer: [L, B, kvh, cap, dh] bf16."""
+
+    def __init__(self, cfg, batch, cap, device):
+        self.cap, self.batch = cap, batch
+        shape = (cfg.L, batch, cfg.kvh, cap, cfg.dh)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+
+
+class _Proj:
+    """One packed projection: codes and fp16 scales of [N, K] in the kernel layout."""
+    __slots__ = ("fmt", "codes", "scales", "N", "K")
+
+    def __init__(self, W, fmt):
+        self.N, self.K = W.shape
+        self.fmt = fmt
+        if fmt == FMT_INT4_G128:
+            self.codes, self.scales, _ = Kn.quant_int4_g128(W, want_scale32=False)
+        else:
+            self.codes, self.scales, _ = Kn.quant_int8_rows(W, want_scale32=False)
+
+    def __call__(self, x, out=None, accumulate=False, static=False):
+        return Kn.linear(self.fmt, x, self.codes, self.scales, self.N, out=out, accumulate=accumulate,
+                         static_weights=static)
+
+    def dequantized(self):
+        return Kn.dequant(self.fmt, self.codes, self.scales, self.N, self.K)
+
+
+class QuantDecoder:
+    """The decoder of configs[3] with packed low-bit projections (see the module docstring)."""
+
+    def __init__(self, cfg=None, device="cuda", fmt="int4", seed=0):
+        self.cfg = cfg = cfg or DecoderConfig()
+        self.dev = torch.device(device)
+        if fmt not in ("int4", "int8"):
+            raise LowbitError(LB_E_ARG, f"projection format '{fmt}' is not int4 or int8")
+        self.fmt = FMT_INT4_G128 if fmt == "int4" else FMT_INT8_ROW
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+        width = (cfg.nh + 2 * cfg.kvh) * cfg.dh
+
+        def proj(n, k):
+            W = torch.randn((n, k), generator=g, device=self.dev) * cfg.wstd
+            p = _Proj(W, self.fmt)
+            del W
+            return p
+
+        self.embed = (torch.randn((cfg.V, cfg.H), generator=g, device=self.dev) * cfg.wstd * 50).to(torch.bfloat16)
+        self.layers = []
+        for _ in range(cfg.L):
+            self.layers.append({
+                "ln1": torch.ones(cfg.H, dtype=torch.bfloat16, device=self.dev),
+                "qkv": proj(width, cfg.H),
+                "o": proj(cfg.H, cfg.nh * cfg.dh),
+                "ln2": torch.ones(cfg.H, dtype=torch.bfloat16, device=self.dev),
+                "gu": proj(2 * cfg.I, cfg.H),
+                "down": proj(cfg.H, cfg.I),
+            })
+        self.norm = torch.ones(cfg.H, dtype=torch.bfloat16, device=self.dev)
+        self.head = proj(cfg.V, cfg.H)
+        half = cfg.dh // 2
+        self._inv = 1.0 / (cfg.theta ** (torch.arange(half, device=self.dev, dtype=torch.float32) / half))
+        self._graph = None
+
+    # ------------------------------------------------------------------ pieces
+    def weight_bytes(self):
+        n = sum(p.codes.numel() + 2 * p.scales.numel() for Ld in self.layers for p in
+                (Ld["qkv"], Ld["o"], Ld["gu"], Ld["down"]))
+        return n + self.head.codes.numel() + 2 * self.head.scales.numel()
+
+    def new_cache(self, batch, cap):
+        return KVCache(self.cfg, batch, cap, self.dev)
+
+    def _rope(self, t, pos):
+        """t: [B, T, h, dh] bf16, pos: [T] or [B, T] int64 -> rotated (float32 arithmetic, half-split pairs)."""
+        ang = pos.to(torch.float32)[..., None] * self._inv            # [.., T, dh/2]
+        if ang.dim() == 2:
+            ang = ang[None]
+        cos, sin = torch.cos(ang)[:, :, None, :], torch.sin(ang)[:, :, None, :]
+        x = t.float()
+        h = x.shape[-1] // 2
+        a, b = x[..., :h], x[..., h:]
+        return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1).to(torch.bfloat16)
+
+    def _block(self, i, X, B, T, cache, pos, start, mask):
+        """One layer on X [B*T, H] (updated in place); pos [T] positions, start: first cache slot (int) or None
+        when pos is a device tensor (decode, captured)."""
+        cfg, Ld = self.cfg, self.layers[i]
+        M = B * T
+        static = M <= 16
+        xn = Kn.rmsnorm(X, Ld["ln1"], eps=cfg.eps)
+        qkv = Ld["qkv"](xn, static=static)
+        q, k, v = qkv.view(B, T, -1).split([cfg.nh * cfg.dh, cfg.kvh * cfg.dh, cfg.kvh * cfg.dh], dim=-1)
+        q = self._rope(q.reshape(B, T, cfg.nh, cfg.dh), pos)
+        k = self._rope(k.reshape(B, T, cfg.kvh, cfg.dh), pos)
+        v = v.reshape(B, T, cfg.kvh, cfg.dh)
+        kc, vc = cache.k[i], cache.v[i]                                # [B, kvh, cap, dh]
+        if start is not None:
+            kc[:, :, start:start + T] = k.transpose(1, 2)
+            vc[:, :, start:start + T] = v.transpose(1, 2)
+            keys, vals = kc[:, :, :start + T], vc[:, :, :start + T]
+            attn = F.scaled_dot_product_attention(q.transpose(1, 2), keys, vals, is_causal=(start == 0 and T > 1),
+                                                  enable_gqa=True)
+        else:                                                          # decode: T == 1, pos is a device tensor
+            kc.index_copy_(2, pos, k.transpose(1, 2))
+            vc.index_copy_(2, pos, v.transpose(1, 2))
+            attn = F.scaled_dot_product_attention(q.transpose(1, 2), kc, vc, attn_mask=mask, enable_gqa=True)
+        o_in = attn.transpose(1, 2).reshape(M, cfg.nh * cfg.dh).contiguous()
+        Ld["o"](o_in, out=X, accumulate=True, static=static)
+        xn2 = Kn.rmsnorm(X, Ld["ln2"], eps=cfg.eps)
+        gu = Ld["gu"](xn2, static=static)
+        g_, u_ = gu.split(cfg.I, dim=-1)
+        m = (F.silu(g_.float()) * u_.float()).to(torch.bfloat16)
+        Ld["down"](m, out=X, accumulate=True, static=static)
+
+    def _logits(self, X_last):
+        xn = Kn.rmsnorm(X_last.contiguous(), self.norm, eps=self.cfg.eps)
+        return self.head(xn, static=X_last.shape[0] <= 16)
+
+    # ------------------------------------------------------------------ forward passes
+    def prefill(self, ids, cache):
+        """ids [B, T] -> logits [B, V] of the last position; fills cache slots [0, T)."""
+        B, T = ids.shape
+        X = self.embed.index_select(0, ids.reshape(-1)).contiguous()   # [B*T, H]
+        pos = torch.arange(T, device=self.dev)
+        for i in range(self.cfg.L):
+            self._block(i, X, B, T, cache, pos, 0, None)
+        return self._logits(X.view(B, T, -1)[:, -1])
+
+    def decode_step(self, tok, cache, pos_t):
+        """tok [B] int64, pos_t [1] int64 (device) -> logits [B, V]; writes cache slot pos_t."""
+        B = tok.shape[0]
+        X = self.embed.index_select(0, tok).contiguous()
+        mask = (torch.arange(cache.cap, device=self.dev) <= pos_t)[None, None, None, :]
+        for i in range(self.cfg.L):
+            self._block(i, X, B, 1, cache, pos_t, None, mask)
+        return self._logits(X)
+
+    def generate(self, ids, steps, graph=True):
+        """Greedy decoding: prefill ids [B, T], then `steps` tokens.  Returns (tokens [B, steps], timings)."""
+        B, T = ids.shape
+        cache = self.new_cache(B, T + steps)
+        torch.cuda.synchronize(self.dev)
+        t0 = time.perf_counter()
+        logits = self.prefill(ids, cache)
+        tok = logits.float().argmax(-1)
+        torch.cuda.synchronize(self.dev)
+        t1 = time.perf_counter()
+        out = torch.empty((B, steps), dtype=torch.int64, device=self.dev)
+        tok_buf = tok.clone()
+        pos_buf = torch.full((1,), T, dtype=torch.int64, device=self.dev)
+        g = None
+        if graph and steps > 0:
+            s = torch.cuda.Stream(device=self.dev)
+            s.wait_stream(torch.cuda.current_stream(self.dev))
+            with torch.cuda.stream(s):                      # warm the kernels' lazy setup outside capture
+                self.decode_step(tok_buf, self.new_cache(B, T + steps), pos_buf)
+            torch.cuda.current_stream(self.dev).wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                logits_buf = self.decode_step(tok_buf, cache, pos_buf)
+                next_tok = logits_buf.float().argmax(-1)
+        torch.cuda.synchronize(self.dev)
+        t2 = time.perf_counter()
+        for s_ in range(steps):
+            if g is not None:
+                g.replay()
+                out[:, s_] = next_tok
+                tok_buf.copy_(next_tok)
+            else:
+                lg = self.decode_step(tok_buf, cache, pos_buf)
+                nt = lg.float().argmax(-1)
+                out[:, s_] = nt
+                tok_buf.copy_(nt)
+            pos_buf += 1
+        torch.cuda.synchronize(self.dev)
+        t3 = time.perf_counter()
+        del g
+        return out, {"prefill_s": t1 - t0, "decode_s": t3 - t2, "capture_s": t2 - t1,
+                     "prefill_tokens": B * T, "decode_tokens": B * steps}
