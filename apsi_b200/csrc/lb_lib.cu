@@ -6,3 +6,4 @@
 #include "lb_noalloc.cu"
 #include "lb_peer.cu"
 #include "lb_norm.cu"
+#include "lb_act.cu"

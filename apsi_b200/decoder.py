@@ -13,9 +13,10 @@ apsi/hub_models.py:1018-1092), one block per layer:
 
 All projections -- QKV, O, gate/up, down and the LM head -- are int4 group-128 (or int8 per-row) weights in
 the library's packed layout, multiplied by ``kernels.linear``: the decode GEMV for up to 16 rows, the tcgen05
-GEMM above; the residual adds are the kernels' accumulate epilogue and the norms ``lb_rmsnorm``.  Embedding
-lookup, rotary position embedding, attention over the KV cache and the SwiGLU product are torch operations:
-they are not on the quantized-linear path this library rebuilds.  Activations are bf16; the KV cache is bf16.
+GEMM above; the residual adds are the kernels' accumulate epilogue.  The norms (``lb_rmsnorm``), the QKV split
+with rotary embedding and the cache write (``lb_qkv_prep``) and the SwiGLU product (``lb_act_mul``) are the
+library's kernels too.  Embedding lookup and attention over the KV cache are torch operations (attention is not
+on the quantized-linear path this library rebuilds).  Activations are bf16; the KV cache is bf16.
 
 Weights are random (seeded, N(0, 0.02) projections, unit norms), as configs[3] specifies; there is no
 checkpoint.  ``generate`` prefills a batch of prompts and then decodes greedily, one CUDA-graph replay per
@@ -82,7 +83,7 @@ class _Proj:
 class QuantDecoder:
     """The decoder of configs[3] with packed low-bit projections (see the module docstring)."""
 
-    def __init__(self, cfg=None, device="cuda", fmt="int4", seed=0):
+    def __init__(self, cfg=None, device="cuda", fmt="int4", seed=0, max_positions=8192):
         self.cfg = cfg = cfg or DecoderConfig()
         self.dev = torch.device(device)
         if fmt not in ("int4", "int8"):
@@ -113,7 +114,9 @@ class QuantDecoder:
         self.head = proj(cfg.V, cfg.H)
         half = cfg.dh // 2
         self._inv = 1.0 / (cfg.theta ** (torch.arange(half, device=self.dev, dtype=torch.float32) / half))
-        self._graph = None
+        ang = torch.arange(max_positions, device=self.dev, dtype=torch.float32)[:, None] * self._inv[None, :]
+        self._cos, self._sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()   # [positions, dh / 2]
+        self.max_positions = max_positions
 
     # ------------------------------------------------------------------ pieces
     def weight_bytes(self):
@@ -122,18 +125,9 @@ class QuantDecoder:
         return n + self.head.codes.numel() + 2 * self.head.scales.numel()
 
     def new_cache(self, batch, cap):
+        if cap > self.max_positions:
+            raise LowbitError(LB_E_ARG, f"a cache of {cap} positions exceeds max_positions ({self.max_positions})")
         return KVCache(self.cfg, batch, cap, self.dev)
-
-    def _rope(self, t, pos):
-        """t: [B, T, h, dh] bf16, pos: [T] or [B, T] int64 -> rotated (float32 arithmetic, half-split pairs)."""
-        ang = pos.to(torch.float32)[..., None] * self._inv            # [.., T, dh/2]
-        if ang.dim() == 2:
-            ang = ang[None]
-        cos, sin = torch.cos(ang)[:, :, None, :], torch.sin(ang)[:, :, None, :]
-        x = t.float()
-        h = x.shape[-1] // 2
-        a, b = x[..., :h], x[..., h:]
-        return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1).to(torch.bfloat16)
 
     def _block(self, i, X, B, T, cache, pos, start, mask):
         """One layer on X [B*T, H] (updated in place); pos [T] positions, start: first cache slot (int) or None
@@ -143,27 +137,20 @@ class QuantDecoder:
         static = M <= 16
         xn = Kn.rmsnorm(X, Ld["ln1"], eps=cfg.eps)
         qkv = Ld["qkv"](xn, static=static)
-        q, k, v = qkv.view(B, T, -1).split([cfg.nh * cfg.dh, cfg.kvh * cfg.dh, cfg.kvh * cfg.dh], dim=-1)
-        q = self._rope(q.reshape(B, T, cfg.nh, cfg.dh), pos)
-        k = self._rope(k.reshape(B, T, cfg.kvh, cfg.dh), pos)
-        v = v.reshape(B, T, cfg.kvh, cfg.dh)
         kc, vc = cache.k[i], cache.v[i]                                # [B, kvh, cap, dh]
+        q = torch.empty((B, cfg.nh, T, cfg.dh), dtype=torch.bfloat16, device=self.dev)
+        Kn.qkv_prep(qkv, B, T, cfg.nh, cfg.kvh, cfg.dh, cfg.dh, self._cos, self._sin, q, kc, vc,
+                    pos0=(pos if start is None else None), start=(start or 0))
         if start is not None:
-            kc[:, :, start:start + T] = k.transpose(1, 2)
-            vc[:, :, start:start + T] = v.transpose(1, 2)
             keys, vals = kc[:, :, :start + T], vc[:, :, :start + T]
-            attn = F.scaled_dot_product_attention(q.transpose(1, 2), keys, vals, is_causal=(start == 0 and T > 1),
-                                                  enable_gqa=True)
+            attn = F.scaled_dot_product_attention(q, keys, vals, is_causal=(start == 0 and T > 1), enable_gqa=True)
         else:                                                          # decode: T == 1, pos is a device tensor
-            kc.index_copy_(2, pos, k.transpose(1, 2))
-            vc.index_copy_(2, pos, v.transpose(1, 2))
-            attn = F.scaled_dot_product_attention(q.transpose(1, 2), kc, vc, attn_mask=mask, enable_gqa=True)
+            attn = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=True)
         o_in = attn.transpose(1, 2).reshape(M, cfg.nh * cfg.dh).contiguous()
         Ld["o"](o_in, out=X, accumulate=True, static=static)
         xn2 = Kn.rmsnorm(X, Ld["ln2"], eps=cfg.eps)
         gu = Ld["gu"](xn2, static=static)
-        g_, u_ = gu.split(cfg.I, dim=-1)
-        m = (F.silu(g_.float()) * u_.float()).to(torch.bfloat16)
+        m = Kn.act_mul(gu, cfg.I, 0)
         Ld["down"](m, out=X, accumulate=True, static=static)
 
     def _logits(self, X_last):

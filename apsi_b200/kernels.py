@@ -299,3 +299,33 @@ def rmsnorm(x, w, eps=1e-6, off=0.0, out=None):
         _lib.call("lb_rmsnorm", _ptr(x), M, K, _ptr(w), wdt, ctypes.c_float(eps), ctypes.c_float(off), _ptr(out),
                   _stream(x.device))
     return out
+
+
+def qkv_prep(qkv, B, T, nh, kvh, dh, rot, cos, sin, q_out, k_cache, v_cache, pos0=None, start=0, qn=None, kn=None,
+             eps=1e-6):
+    """Split / (optionally) RMSNorm / rotate the fused QKV projection; q_out [B, nh, T, dh]; k_cache, v_cache
+    [B, kvh, cap, dh] written at positions pos0 + t (device int64 tensor) or start + t.  See lb_qkv_prep."""
+    _need_cuda(qkv, "qkv")
+    if qkv.dtype != torch.bfloat16 or not qkv.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "qkv must be a contiguous bfloat16 tensor")
+    for t, n in ((q_out, "q_out"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise LowbitError(_lib.LB_E_ARG, f"{n} must be a contiguous bfloat16 tensor")
+    cap = k_cache.shape[-2]
+    with torch.cuda.device(qkv.device):
+        _lib.call("lb_qkv_prep", _ptr(qkv), B, T, nh, kvh, dh, rot, _ptr(cos), _ptr(sin), _ptr(qn), _ptr(kn),
+                  ctypes.c_float(eps), _ptr(pos0), int(start), _ptr(q_out), nh * T * dh, dh, T * dh,
+                  _ptr(k_cache), _ptr(v_cache), kvh * cap * dh, cap * dh, _stream(qkv.device))
+
+
+def act_mul(gu, I, kind=0, out=None):
+    """act(g) * u of the fused [g | u] projection gu [M, 2 I] (bf16); kind 0 silu, 1 gelu (tanh form)."""
+    _need_cuda(gu, "gu")
+    if gu.dtype != torch.bfloat16 or not gu.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "gu must be a contiguous bfloat16 tensor")
+    M = gu.numel() // (2 * I)
+    if out is None:
+        out = torch.empty((M, I), dtype=torch.bfloat16, device=gu.device)
+    with torch.cuda.device(gu.device):
+        _lib.call("lb_act_mul", _ptr(gu), M, I, kind, _ptr(out), _stream(gu.device))
+    return out

@@ -590,8 +590,8 @@ def decoder_measure(torch, dev, hbm_peak, batch=8, prompt=512, steps=128):
            "decode_weight_GB_per_s": round(wb / step_s / 1e9, 1),
            "decode_weight_hbm_frac": round(wb / step_s / 1e9 / hbm_peak, 4),
            "weight_bytes": wb, "model_build_s": round(build_s, 2),
-           "note": "embedding, RoPE, attention and SwiGLU are torch ops; every projection and RMSNorm is this "
-                   "library's"}
+           "note": "embedding lookup and attention are torch ops; every projection, RMSNorm, the QKV split with "
+                   "RoPE and cache write, and SwiGLU are this library's kernels"}
     del model, toks
     torch.cuda.empty_cache()
     return res

@@ -125,6 +125,23 @@ int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, 
 int lb_rmsnorm(const void* x, int64_t M, int64_t K, const void* w, int w_dtype, float eps, float off, void* out,
                void* stream);
 
+/* The step between a decoder's fused QKV projection and its attention: split the [B T, (nh + 2 kvh) dh] bf16
+ * projection into heads; optionally RMSNorm every q / k head (qn, kn: bf16 [dh] weights, or NULL); rotate the
+ * first `rot` values of every q and k head with half-split pairs [a cos - b sin, b cos + a sin] (a = v[:rot/2],
+ * b = v[rot/2:rot]; cos, sin: float32 tables [positions, rot/2]); write q[b, h, t, :] at
+ * q + b q_sb + t q_st + h q_sh (elements) and k, v of token t into the caches at position p = *pos0 + t (pos0: a
+ * device int64, so a captured graph can advance it) or start + t when pos0 is NULL:
+ * cache[b, h, p, :] at b c_sb + h c_sh + p dh.  Float32 arithmetic, bf16 results.  Replaces hub_gpu's
+ * qkv_prep op (apsi/hub_gpu.py:1547-1552, host form 1701-1723). */
+int lb_qkv_prep(const void* qkv, int B, int T, int nh, int kvh, int dh, int rot, const float* cos, const float* sin,
+                const void* qn, const void* kn, float eps, const int64_t* pos0, int64_t start, void* q,
+                int64_t q_sb, int64_t q_st, int64_t q_sh, void* k_cache, void* v_cache, int64_t c_sb, int64_t c_sh,
+                void* stream);
+/* out[m, i] = act(gu[m, i]) * gu[m, I + i] for the fused [g | u] gate/up projection (bf16 [M, 2 I] -> [M, I]);
+ * kind 0: silu g / (1 + exp(-g)); kind 1: gelu, tanh form.  Replaces hub_gpu's act_mul op
+ * (apsi/hub_gpu.py:1598-1600, host form 1755-1762). */
+int lb_act_mul(const void* gu, int64_t M, int64_t I, int kind, void* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- products */
 
 /* Bytes of device workspace lb_linear needs for this shape (0 when none).  Replaces the scratch buffers of

@@ -19,6 +19,8 @@ Formats restated (reference file:line in ATECTechnologies/apsi):
 * ggml-style blocks of 32 (``hub_gpu.qnumpy``) -- ``apsi/hub_gpu.py:1215-1241``; the device word layout of
   those codes -- ``apsi/hub_gpu.py:786-800`` (int8: byte j of a word = value j; int4: nibble j = q + 8).
 """
+import math
+
 import numpy as np
 
 __all__ = [
@@ -142,6 +144,35 @@ def rms_norm(x, w, eps=1e-6, off=0.0):
     x = np.asarray(x, np.float32)
     w = np.asarray(w, np.float32)
     return (x / np.sqrt((x * x).mean(-1, keepdims=True) + np.float32(eps)) * (w + np.float32(off))).astype(np.float32)
+
+
+def qkv_prep(qkv, cos, sin, qn, kn, nh, kvh, dh, rot, start, eps):
+    """The reference host qkv_prep (apsi/hub_gpu.py:1701-1723) for one sequence: qkv [T, (nh + 2 kvh) dh]
+    float32, cos / sin [positions, rot / 2] -> q [T, nh, dh], k [T, kvh, dh], v [T, kvh, dh] (float32)."""
+    qkv = np.asarray(qkv, np.float32)
+    T = qkv.shape[0]
+    x = qkv.reshape(T, nh + 2 * kvh, dh)
+    half = rot // 2
+    c = np.asarray(cos, np.float32)[start:start + T].reshape(T, 1, half)
+    s = np.asarray(sin, np.float32)[start:start + T].reshape(T, 1, half)
+
+    def prep(v, w):
+        if w is not None:
+            v = v / np.sqrt((v * v).mean(-1, keepdims=True) + np.float32(eps)) * np.asarray(w, np.float32)[:dh]
+        r1, r2, rest = v[..., :half], v[..., half:rot], v[..., rot:]
+        return np.concatenate([r1 * c - r2 * s, r2 * c + r1 * s, rest], -1)
+    return prep(x[:, :nh], qn), prep(x[:, nh:nh + kvh], kn), x[:, nh + kvh:]
+
+
+def act_mul(gu, I, kind):
+    """The reference host act_mul (apsi/hub_gpu.py:1755-1762): silu(g) * u (kind 0) or tanh-gelu(g) * u."""
+    gu = np.asarray(gu, np.float32)
+    g, u = gu[:, :I], gu[:, I:]
+    if kind == 0:
+        a = g / (1 + np.exp(-g))
+    else:
+        a = 0.5 * g * (1 + np.tanh(math.sqrt(2 / math.pi) * (g + 0.044715 * g ** 3)))
+    return (a * u).astype(np.float32)
 
 
 def qmatmul_dequant_reference(x, packed_or_codes, scale16, fmt):
