@@ -18,6 +18,9 @@ Formats restated (reference file:line in ATECTechnologies/apsi):
 * quantized product -- ``apsi/precision.py:294-299`` (``qmatmul``): dequantise and multiply.
 * ggml-style blocks of 32 (``hub_gpu.qnumpy``) -- ``apsi/hub_gpu.py:1215-1241``; the device word layout of
   those codes -- ``apsi/hub_gpu.py:786-800`` (int8: byte j of a word = value j; int4: nibble j = q + 8).
+* minifloat formats (fp8 e4m3 / e5m2, fp6 e3m2 / e2m3, fp4 e2m1) -- ``apsi/precision.py:23-138, 182-246``:
+  value tables, round-to-nearest-even onto the grid with saturation, 6-bit packing, per-row / per-tensor scales.
+* GGUF Q8_0 / Q4_0 block bytes -- ``apsi/modelio.py:56-95``.
 """
 import math
 
@@ -28,6 +31,8 @@ __all__ = [
     "quant_int8_rows", "quant_int4_g128", "dequant_int8_rows", "dequant_int4_g128", "linear_ref",
     "qnumpy_g32", "pack_q4_0_words", "pack_q8_0_words", "dequant_g32", "rel_frobenius", "max_abs_ratio",
     "make_config_inputs", "qmatmul_dequant_reference", "round_weights_g32",
+    "MINIFLOATS", "minifloat_table", "minifloat_max", "minifloat_encode", "minifloat_decode", "pack6", "unpack6",
+    "quant_minifloat", "dequant_minifloat", "gguf_q8_0", "gguf_q4_0", "gguf_dequant",
 ]
 
 
@@ -241,6 +246,170 @@ def dequant_g32(q, sc):
     O, I = q.shape
     return (np.asarray(q, np.float32).reshape(O, I // 32, 32) * np.asarray(sc, np.float32)[:, :, None]) \
         .reshape(O, I).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------- minifloats
+# (exp_bits, man_bits, bias, finite_only, nan_top) of the reference's minifloat formats, apsi/precision.py:70-76
+MINIFLOATS = {
+    "fp8_e4m3": (4, 3, 7, True, True),
+    "fp8_e5m2": (5, 2, 15, False, False),
+    "fp6_e3m2": (3, 2, 3, True, False),
+    "fp6_e2m3": (2, 3, 1, True, False),
+    "fp4_e2m1": (2, 1, 1, True, False),
+}
+
+
+def minifloat_table(name):
+    """Value of every magnitude code (apsi/precision.py:23-39): subnormals at exponent field 0, inf / NaN in
+    the top exponent unless the format is finite-only, the all-ones code NaN when ``nan_top``."""
+    eb, mb, bias, finite_only, nan_top = MINIFLOATS[name]
+    top = (1 << eb) - 1
+    out = []
+    for code in range(1 << (eb + mb)):
+        e, m = code >> mb, code & ((1 << mb) - 1)
+        v = math.ldexp(m, 1 - bias - mb) if e == 0 else math.ldexp((1 << mb) + m, e - bias - mb)
+        if not finite_only and e == top:
+            v = math.inf if m == 0 else math.nan
+        if nan_top and e == top and m == (1 << mb) - 1:
+            v = math.nan
+        out.append(v)
+    return np.array(out)
+
+
+def minifloat_max(name):
+    t = minifloat_table(name)
+    return float(np.max(t[np.isfinite(t)]))
+
+
+def minifloat_encode(name, y):
+    """Codes of float64 values on the format's grid (apsi/precision.py:109-130): round to nearest with ties to the
+    even code (the even mantissa), magnitudes above the largest finite value saturate, the sign bit follows
+    signbit (so -0.0 keeps it), NaN takes the format's first NaN code, or the all-ones magnitude when the
+    format has no NaN.  Restated with exponent arithmetic: the quotient by the ulp of the value's binade
+    (the subnormal ulp below the smallest normal) is rounded half-to-even."""
+    eb, mb, bias, _, _ = MINIFLOATS[name]
+    y = np.asarray(y, np.float64)
+    sign = np.signbit(y)
+    a = np.minimum(np.abs(y), minifloat_max(name))
+    nan = np.isnan(y)
+    a = np.where(nan, 0.0, a)
+    _, ex = np.frexp(a)
+    e = np.where(a > 0, np.maximum(ex - 1, 1 - bias), 1 - bias)   # binade exponent; the smallest normal one for
+                                                                  # subnormals and zero
+    r = np.rint(np.ldexp(a, -(e - mb)))                  # exact power-of-two scaling, round half to even
+    code = ((e + bias).astype(np.int64) << mb) + r.astype(np.int64) - (1 << mb)
+    code = code | (sign.astype(np.int64) << (eb + mb))
+    if nan.any():
+        t = minifloat_table(name)
+        nan_code = int(np.argmax(np.isnan(t))) if np.isnan(t).any() else (1 << (eb + mb)) - 1
+        code = np.where(nan, nan_code, code)
+    return code.astype(np.uint8)
+
+
+def minifloat_decode(name, codes):
+    """float32 values of codes (apsi/precision.py:133-138)."""
+    eb, mb = MINIFLOATS[name][:2]
+    codes = np.asarray(codes).astype(np.int64)
+    mag = minifloat_table(name)[codes & ((1 << (eb + mb)) - 1)]
+    return (mag * np.where((codes >> (eb + mb)) & 1, -1.0, 1.0)).astype(np.float32)
+
+
+def pack6(codes):
+    """Four 6-bit codes per three bytes, little-endian 24-bit words, zero-padded (apsi/precision.py:182-192)."""
+    flat = np.asarray(codes).reshape(-1).astype(np.uint32) & 0x3F
+    flat = np.concatenate([flat, np.zeros((-flat.size) % 4, np.uint32)])
+    g = flat.reshape(-1, 4)
+    word = g[:, 0] | (g[:, 1] << 6) | (g[:, 2] << 12) | (g[:, 3] << 18)
+    return np.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], axis=1).astype(np.uint8).reshape(-1)
+
+
+def unpack6(packed, n):
+    b = np.asarray(packed, np.uint8).reshape(-1, 3).astype(np.uint32)
+    word = b[:, 0] | (b[:, 1] << 8) | (b[:, 2] << 16)
+    return np.stack([(word >> (6 * k)) & 0x3F for k in range(4)], axis=1).astype(np.uint8).reshape(-1)[:n]
+
+
+def quant_minifloat(x, name, axis):
+    """``precision.quantize(x, name, axis=axis)`` for a minifloat format (apsi/precision.py:205-246).
+
+    axis=0 on a 2-D array: one float32 scale per row, ``max|row| / fmt.max`` (1.0 when the maximum is zero or
+    NaN); axis=None: one float64 scale for the tensor.  Codes of ``x64 / scale`` flat in row-major order,
+    packed for the 4- and 6-bit formats.  Returns (codes, scale)."""
+    xv = np.asarray(x, np.float64)
+    fmax = minifloat_max(name)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        return _quant_minifloat(xv, name, axis, fmax)
+
+
+def _quant_minifloat(xv, name, axis, fmax):
+    if axis is None:
+        m = float(np.max(np.abs(xv))) if xv.size else 0.0
+        s = m / fmax if m > 0 else 1.0
+        y = xv / s
+    else:
+        m = np.max(np.abs(xv), axis=1, keepdims=True)
+        s = np.where(m > 0, m / fmax, 1.0).astype(np.float32)
+        y = xv / s
+    codes = minifloat_encode(name, y).reshape(-1)
+    bits = {"fp8": 8, "fp6": 6, "fp4": 4}[name[:3]]
+    if bits == 4:
+        codes = pack4(codes)
+    elif bits == 6:
+        codes = pack6(codes)
+    return codes, s
+
+
+def dequant_minifloat(codes, name, shape, scale):
+    """``precision.dequantize`` of a minifloat QTensor: ``decode(code) * float32(scale)`` (precision.py:249-274)."""
+    n = int(np.prod(shape))
+    bits = {"fp8": 8, "fp6": 6, "fp4": 4}[name[:3]]
+    c = np.asarray(codes, np.uint8).reshape(-1)
+    if bits == 4:
+        c = unpack4(c, n)
+    elif bits == 6:
+        c = unpack6(c, n)
+    v = minifloat_decode(name, c[:n]).reshape(shape)
+    with np.errstate(invalid="ignore"):
+        return (v * np.asarray(scale, np.float32)).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------- GGUF Q8_0 / Q4_0
+def gguf_q8_0(a):
+    """ggml Q8_0 blocks of 32 (apsi/modelio.py:56-67): binary16 d = amax / 127 (float32 arithmetic), then the 32
+    int8 codes sign(y) * floor(|y| + 0.5) of y = x * (1 / d) (0 when d == 0), all in float32."""
+    x = np.asarray(a, np.float32).reshape(-1, 32)
+    d = (np.max(np.abs(x), axis=1) / np.float32(127.0)).astype(np.float32)
+    inv = np.zeros_like(d)
+    np.divide(np.float32(1.0), d, out=inv, where=d != 0)
+    y = x * inv[:, None]
+    q = (np.sign(y) * np.floor(np.abs(y) + np.float32(0.5))).astype(np.int8)
+    return np.concatenate([d.astype(np.float16).view(np.uint8).reshape(-1, 2), q.view(np.uint8)], axis=1).reshape(-1)
+
+
+def gguf_q4_0(a):
+    """ggml Q4_0 blocks of 32 (apsi/modelio.py:70-81): d = x[argmax|x|] / -8 (the first largest magnitude, signed),
+    codes min(15, trunc(x * (1 / d) + 8.5)) in float32, value j in the low nibble of byte j, value j + 16 in its
+    high nibble."""
+    x = np.asarray(a, np.float32).reshape(-1, 32)
+    mx = x[np.arange(x.shape[0]), np.argmax(np.abs(x), axis=1)]
+    d = (mx / np.float32(-8.0)).astype(np.float32)
+    inv = np.zeros_like(d)
+    np.divide(np.float32(1.0), d, out=inv, where=d != 0)
+    q = np.minimum(15, (x * inv[:, None] + np.float32(8.5)).astype(np.int8)).astype(np.uint8)
+    body = q[:, :16] | (q[:, 16:] << 4)
+    return np.concatenate([d.astype(np.float16).view(np.uint8).reshape(-1, 2), body], axis=1).reshape(-1)
+
+
+def gguf_dequant(buf, kind, n):
+    """float32 values of Q8_0 / Q4_0 blocks (apsi/modelio.py:84-95)."""
+    b = np.asarray(buf, np.uint8).reshape(-1, 34 if kind == "q8_0" else 18)
+    d = b[:, :2].copy().view(np.float16).astype(np.float32)
+    if kind == "q8_0":
+        v = b[:, 2:].view(np.int8).astype(np.float32)
+    else:
+        v = np.concatenate([(b[:, 2:] & 0x0F).astype(np.int8) - 8, (b[:, 2:] >> 4).astype(np.int8) - 8],
+                           axis=1).astype(np.float32)
+    return (v * d).reshape(-1)[:n]
 
 
 # ------------------------------------------------------------------------------------------- error metrics

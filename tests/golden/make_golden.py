@@ -134,6 +134,68 @@ def main():
     modelio.save_model(apsim, tree, metadata={"written_by": "apsi.modelio.save_model"})
     print("wrote", apsim)
 
+    # ---- minifloat formats (precision.quantize with scale="auto"): per row (axis=0) and per tensor (axis=None).
+    # Rows whose absmax is the format's largest value are quantised with scale 1.0 exactly, so they carry exact
+    # grid midpoints (ties), values one float32 ulp beside them, subnormal-range values and signed zeros; a row
+    # with a NaN (scale 1.0, other values saturate), a row with an infinity (scale inf), an all-zero row, and
+    # seeded normal rows.
+    for name in ("fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1"):
+        f = precision.get_format(name)
+        vals = np.asarray(f.sorted_vals, np.float64)
+        mids = (vals[:-1] + vals[1:]) / 2.0
+        C = 96
+        rows = []
+        for arr in (mids, np.nextafter(mids.astype(np.float32), np.float32(np.inf)),
+                    np.nextafter(mids.astype(np.float32), np.float32(-np.inf)), vals):
+            r = np.resize(np.asarray(arr, np.float64), C)
+            r[1::3] *= -1.0
+            r[0] = f.max
+            rows.append(r.astype(np.float32))
+        z = np.zeros(C, np.float32)
+        z[1::2] = -0.0
+        z[0] = f.max
+        z[3] = np.float32(vals[1] / 3.0)                    # below half the smallest subnormal
+        z[4] = np.float32(vals[1] / 2.0)                    # exactly half of it (tie with zero)
+        rows.append(z)
+        nanrow = (rng.standard_normal(C) * 3 * f.max).astype(np.float32)
+        nanrow[7] = np.nan
+        rows.append(nanrow)
+        infrow = (rng.standard_normal(C)).astype(np.float32)
+        infrow[11] = -np.inf
+        rows.append(infrow)
+        rows.append(np.zeros(C, np.float32))
+        for _ in range(6):
+            rows.append((rng.standard_normal(C) * 0.02).astype(np.float32))
+        o = (rng.standard_normal(C) * 0.02).astype(np.float32)
+        o[::17] *= 200.0
+        rows.append(o)
+        Wm = np.stack(rows)
+        q = precision.quantize(Wm, name, axis=0)
+        out[f"mf_{name}_w"] = Wm
+        out[f"mf_{name}_codes"] = np.asarray(q.codes, np.uint8).reshape(-1)
+        out[f"mf_{name}_scale"] = np.asarray(q.scale, np.float32).reshape(-1)
+        out[f"mf_{name}_deq"] = np.asarray(precision.dequantize(q), np.float32)
+        Wt = (rng.standard_normal((7, 37)) * 0.3).astype(np.float32)          # odd sizes: packing runs across rows
+        Wt[2, 5] = -0.0
+        qt = precision.quantize(Wt, name)
+        out[f"mf_{name}_t_w"] = Wt
+        out[f"mf_{name}_t_codes"] = np.asarray(qt.codes, np.uint8).reshape(-1)
+        out[f"mf_{name}_t_scale"] = np.asarray([qt.scale], np.float64)
+        out[f"mf_{name}_t_deq"] = np.asarray(precision.dequantize(qt), np.float32)
+
+    # ---- GGUF Q8_0 / Q4_0 block bytes (apsi/modelio.py:56-95): seeded blocks, ties at half-integers of the
+    # scaled values, an all-zero block, a block whose largest magnitude is negative
+    from apsi import modelio as _mio  # noqa: E402
+    G = (rng.standard_normal((6, 128)) * 0.05).astype(np.float32)
+    G[1, :32] = 0.0
+    G[2, :32] = np.linspace(-1.0, 0.5, 32, dtype=np.float32)
+    G[3, 32:64] = (np.arange(32, dtype=np.float32) - 16.0) * np.float32(0.125) + np.float32(0.0625)
+    out["gguf_w"] = G
+    out["gguf_q8_0"] = np.frombuffer(_mio._q8_0(G), np.uint8).copy()
+    out["gguf_q4_0"] = np.frombuffer(_mio._q4_0(G), np.uint8).copy()
+    out["gguf_dq8_0"] = np.asarray(_mio._dq8_0(out["gguf_q8_0"].tobytes(), G.size), np.float32)
+    out["gguf_dq4_0"] = np.asarray(_mio._dq4_0(out["gguf_q4_0"].tobytes(), G.size), np.float32)
+
     path = os.path.join(HERE, "lowbit_golden.npz")
     np.savez_compressed(path, **out)
     print("wrote", path, {k: v.shape for k, v in out.items()})

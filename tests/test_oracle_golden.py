@@ -1,5 +1,6 @@
 """The oracle against golden vectors written by the reference itself (tests/golden/make_golden.py):
-int4 groups of 128, int8 rows, ggml-style g32 blocks, dequantisation and the quantized product."""
+int4 groups of 128, int8 rows, ggml-style g32 blocks, dequantisation, the quantized product, the minifloat
+formats and the GGUF Q8_0 / Q4_0 blocks."""
 import numpy as np
 
 import oracle as O
@@ -69,3 +70,47 @@ def test_round_weights_matches_reference_lowbit(golden):
     for kind in ("int8", "int4"):
         got = O.round_weights_g32(golden["rw_in"], kind)
         assert np.array_equal(got.view(np.uint32), golden[f"rw_{kind}"].view(np.uint32)), kind
+
+
+MINIFLOAT_NAMES = ("fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1")
+
+
+def test_minifloat_rows_match_reference(golden):
+    """Per-row scales (axis=0): ties to the even code, saturation, NaN / inf rows, signed zeros."""
+    for name in MINIFLOAT_NAMES:
+        W = golden[f"mf_{name}_w"]
+        codes, s = O.quant_minifloat(W, name, 0)
+        np.testing.assert_array_equal(codes, golden[f"mf_{name}_codes"], err_msg=name)
+        np.testing.assert_array_equal(s.reshape(-1), golden[f"mf_{name}_scale"], err_msg=name)
+        d = O.dequant_minifloat(codes, name, W.shape, s)
+        assert np.array_equal(d.view(np.uint32)[~np.isnan(d)], golden[f"mf_{name}_deq"].view(np.uint32)[~np.isnan(d)])
+        np.testing.assert_array_equal(np.isnan(d), np.isnan(golden[f"mf_{name}_deq"]))
+
+
+def test_minifloat_tensor_scale_matches_reference(golden):
+    """One float64 scale for the tensor (axis=None); packing runs across rows for odd sizes."""
+    for name in MINIFLOAT_NAMES:
+        W = golden[f"mf_{name}_t_w"]
+        codes, s = O.quant_minifloat(W, name, None)
+        np.testing.assert_array_equal(codes, golden[f"mf_{name}_t_codes"], err_msg=name)
+        assert s == float(golden[f"mf_{name}_t_scale"][0])
+        d = O.dequant_minifloat(codes, name, W.shape, s)
+        assert np.array_equal(d.view(np.uint32), golden[f"mf_{name}_t_deq"].view(np.uint32)), name
+
+
+def test_minifloat_tables_and_pack6():
+    assert [O.minifloat_max(n) for n in MINIFLOAT_NAMES] == [448.0, 57344.0, 28.0, 7.5, 6.0]
+    t = O.minifloat_table("fp8_e4m3")
+    assert np.isnan(t[0x7F]) and t[1] == 2.0 ** -9 and t[0x08] == 2.0 ** -6
+    c = np.array([1, 2, 3, 63, 5], np.uint8)
+    p = O.pack6(c)
+    assert p.size == 6 and p[0] == (1 | (2 << 6)) & 0xFF
+    np.testing.assert_array_equal(O.unpack6(p, 5), c)
+
+
+def test_gguf_blocks_match_reference(golden):
+    G = golden["gguf_w"]
+    np.testing.assert_array_equal(O.gguf_q8_0(G), golden["gguf_q8_0"])
+    np.testing.assert_array_equal(O.gguf_q4_0(G), golden["gguf_q4_0"])
+    np.testing.assert_array_equal(O.gguf_dequant(golden["gguf_q8_0"], "q8_0", G.size), golden["gguf_dq8_0"])
+    np.testing.assert_array_equal(O.gguf_dequant(golden["gguf_q4_0"], "q4_0", G.size), golden["gguf_dq4_0"])
