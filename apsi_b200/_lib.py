@@ -12,6 +12,9 @@ from .build import LIB_PATH
 LB_OK = 0
 LB_E_ARG, LB_E_ALIGN, LB_E_DEVICE, LB_E_LAUNCH, LB_E_WORKSPACE, LB_E_UNSUPPORTED = -1, -2, -3, -4, -5, -6
 FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32 = 1, 2, 3, 4
+FMT_FP8_E4M3, FMT_FP8_E5M2, FMT_FP6_E3M2, FMT_FP6_E2M3, FMT_FP4_E2M1 = 5, 6, 7, 8, 9
+MINIFLOAT_FMT = {"fp8_e4m3": FMT_FP8_E4M3, "fp8_e5m2": FMT_FP8_E5M2, "fp6_e3m2": FMT_FP6_E3M2,
+                 "fp6_e2m3": FMT_FP6_E2M3, "fp4_e2m1": FMT_FP4_E2M1}
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 DEVERR_WAIT_TIMEOUT = 1
 DEVERR_PEER_TIMEOUT = 2
@@ -36,6 +39,9 @@ SIGNATURES = [
     ("lb_quant_q4_0_g32", _I, [_P, _I, _I64, _I64, _P, _P, _P]),
     ("lb_round_g32", _I, [_I, _P, _I, _I64, _I64, _P, _P]),
     ("lb_dequant", _I, [_I, _P, _P, _I, _I64, _I64, _P, _I, _P]),
+    ("lb_minifloat_bytes", _I64, [_I, _I64]),
+    ("lb_quant_minifloat", _I, [_I, _P, _I, _I64, _I64, _I, _P, _P, _P, _P]),
+    ("lb_dequant_minifloat", _I, [_I, _P, _I64, _I64, _I, _P, ctypes.c_float, _P, _I, _P]),
     ("lb_linear_workspace_size", _I, [_I, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     ("lb_linear", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, _P]),
     ("lb_linear_ex", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, ctypes.c_uint, _P]),

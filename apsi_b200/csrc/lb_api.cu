@@ -221,6 +221,49 @@ int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, 
                   "dequant");
 }
 
+static bool is_minifloat(int fmt) { return fmt >= LB_FMT_FP8_E4M3 && fmt <= LB_FMT_FP4_E2M1; }
+
+int64_t lb_minifloat_bytes(int fmt, int64_t n) {
+  if (!is_minifloat(fmt) || n < 0) return -1;
+  return minifloat_bytes(fmt, n);
+}
+
+int lb_quant_minifloat(int fmt, const void* w, int w_dtype, int64_t R, int64_t C, int per_row, uint8_t* codes,
+                       float* scale32, float* absmax, void* stream) {
+  if (!is_minifloat(fmt)) return fail(LB_E_ARG, "lb_quant_minifloat: %d is not a minifloat format", fmt);
+  if (!w || !codes) return fail(LB_E_ARG, "lb_quant_minifloat: NULL pointer");
+  if (w_dtype != LB_DT_F32 && w_dtype != LB_DT_BF16)
+    return fail(LB_E_ARG, "lb_quant_minifloat: w_dtype must be LB_DT_F32 or LB_DT_BF16");
+  if (R <= 0 || C <= 0) return fail(LB_E_ARG, "lb_quant_minifloat: R and C must be positive");
+  if (per_row ? !scale32 : !absmax)
+    return fail(LB_E_ARG, "lb_quant_minifloat: per_row needs scale32[R], per tensor needs absmax[1]");
+  if (!aligned(w, w_dtype == LB_DT_F32 ? 4 : 2) || !aligned(codes, 8) || (scale32 && !aligned(scale32, 4)) ||
+      (absmax && !aligned(absmax, 4)))
+    return fail(LB_E_ALIGN, "lb_quant_minifloat: w element-aligned, codes 8-byte, scale32 / absmax 4-byte aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_quant_minifloat(fmt, w, w_dtype, R, C, per_row, codes, scale32, absmax, d->sms,
+                                         static_cast<cudaStream_t>(stream)),
+                  "quant_minifloat");
+}
+
+int lb_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, int per_row, const float* scale32,
+                         float tensor_scale, void* out, int out_dtype, void* stream) {
+  if (!is_minifloat(fmt)) return fail(LB_E_ARG, "lb_dequant_minifloat: %d is not a minifloat format", fmt);
+  if (!codes || !out || (per_row && !scale32)) return fail(LB_E_ARG, "lb_dequant_minifloat: NULL pointer");
+  if (out_dtype != LB_DT_F32 && out_dtype != LB_DT_BF16) return fail(LB_E_ARG, "lb_dequant_minifloat: bad out_dtype");
+  if (R <= 0 || C <= 0) return fail(LB_E_ARG, "lb_dequant_minifloat: R and C must be positive");
+  if (!aligned(out, out_dtype == LB_DT_F32 ? 4 : 2) || (scale32 && !aligned(scale32, 4)))
+    return fail(LB_E_ALIGN, "lb_dequant_minifloat: out and scale32 must be element-aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_dequant_minifloat(fmt, codes, R, C, per_row, scale32, tensor_scale, out, out_dtype, d->sms,
+                                           static_cast<cudaStream_t>(stream)),
+                  "dequant_minifloat");
+}
+
 static bool use_gemv(int64_t M) { return M <= 16; }
 
 int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes) {

@@ -37,6 +37,14 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
                         cudaStream_t st, const char** why, const OutRanks* dst = nullptr);
 
+int minifloat_bits(int fmt);
+int64_t minifloat_bytes(int fmt, int64_t n);
+cudaError_t launch_quant_minifloat(int fmt, const void* w, int dt, int64_t R, int64_t C, int per_row,
+                                   uint8_t* codes, float* scale32, float* absmax, int sms, cudaStream_t st);
+cudaError_t launch_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, int per_row,
+                                     const float* scale32, float tscale, void* out, int out_dt, int sms,
+                                     cudaStream_t st);
+
 cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, int sms, cudaStream_t st);
 
 }  // namespace lb

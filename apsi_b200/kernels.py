@@ -13,7 +13,7 @@ from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F3
 
 __all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "round_g32", "dequant", "linear",
            "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
-           "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError"]
+           "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError", "minifloat_bytes", "quant_minifloat", "dequant_minifloat"]
 
 
 def _ptr(t):
@@ -96,6 +96,43 @@ def round_g32(w, fmt):
     out = torch.empty((N, K), dtype=torch.float32, device=w.device)
     with torch.cuda.device(w.device):
         _lib.call("lb_round_g32", fmt, _ptr(w), _weight_dtype(w), N, K, _ptr(out), _stream(w.device))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ minifloats
+def minifloat_bytes(fmt, n):
+    """Bytes of the packed codes of n values in minifloat format ``fmt`` (FMT_FP8_E4M3 .. FMT_FP4_E2M1)."""
+    return int(_lib.load().lb_minifloat_bytes(fmt, n))
+
+
+def quant_minifloat(w, fmt, per_row=True):
+    """precision.quantize(w, <minifloat>, axis=0 if per_row else None) of a 2-D weight on the device.
+
+    Returns (codes, scale): packed uint8 codes (flat row-major) and, per row, the float32 scales [R]; per tensor,
+    a one-element float32 tensor holding max|w| (the tensor scale is max / fmt.max in float64)."""
+    _need_cuda(w, "w")
+    R, C = w.shape
+    codes = torch.empty((minifloat_bytes(fmt, R * C),), dtype=torch.uint8, device=w.device)
+    aux = torch.empty((R if per_row else 1,), dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        _lib.call("lb_quant_minifloat", fmt, _ptr(w), _weight_dtype(w), R, C, 1 if per_row else 0, _ptr(codes),
+                  _ptr(aux) if per_row else ctypes.c_void_p(0), ctypes.c_void_p(0) if per_row else _ptr(aux),
+                  _stream(w.device))
+    return codes, aux
+
+
+def dequant_minifloat(fmt, codes, R, C, scale, out_dtype=torch.float32):
+    """value(code) * scale as [R, C]: ``scale`` a float32 CUDA tensor [R] (per row) or a Python float."""
+    _need_cuda(codes, "codes")
+    out = torch.empty((R, C), dtype=out_dtype, device=codes.device)
+    per_row = isinstance(scale, torch.Tensor)
+    if per_row:
+        _need_cuda(scale, "scale")
+    dt = DT_F32 if out_dtype == torch.float32 else DT_BF16
+    with torch.cuda.device(codes.device):
+        _lib.call("lb_dequant_minifloat", fmt, _ptr(codes), R, C, 1 if per_row else 0,
+                  _ptr(scale) if per_row else ctypes.c_void_p(0), ctypes.c_float(0.0 if per_row else float(scale)),
+                  _ptr(out), dt, _stream(codes.device))
     return out
 
 

@@ -22,7 +22,7 @@ import math
 import numpy as np
 
 from . import kernels as _k
-from ._lib import FMT_INT8_ROW, FMT_INT4_G128, LowbitError
+from ._lib import FMT_INT8_ROW, FMT_INT4_G128, MINIFLOAT_FMT, LowbitError
 
 __all__ = ["RuntimeErr", "Format", "FORMATS", "ALIASES", "get_format", "QTensor", "quantize", "dequantize",
            "round_to", "qmatmul", "nbytes", "quant_error", "format_info", "quantize_linear", "module"]
@@ -33,13 +33,13 @@ class RuntimeErr(Exception):
 
 
 class Format:
-    """A numeric format.  The B200 path implements the integer formats; the table keeps the reference's
-    names so ``get_format`` accepts the same spellings (apsi/precision.py:43-74)."""
+    """A numeric format.  The B200 path implements the integer and the minifloat formats; the table keeps the
+    reference's names so ``get_format`` accepts the same spellings (apsi/precision.py:43-74)."""
 
-    def __init__(self, name, bits, kind, qmax=None):
+    def __init__(self, name, bits, kind, qmax=None, maxval=None):
         self.name, self.bits, self.kind = name, bits, kind
         self.qmax = qmax
-        self.max = float(qmax) if qmax is not None else None
+        self.max = float(qmax) if qmax is not None else maxval
 
     def __repr__(self):
         return self.name
@@ -48,9 +48,15 @@ class Format:
 FORMATS = {
     "int8": Format("int8", 8, "int", qmax=127),
     "int4": Format("int4", 4, "int", qmax=7),
+    # OCP fp8 and MX fp6 / fp4 element formats, largest finite values of the reference's tables
+    "fp8_e4m3": Format("fp8_e4m3", 8, "minifloat", maxval=448.0),
+    "fp8_e5m2": Format("fp8_e5m2", 8, "minifloat", maxval=57344.0),
+    "fp6_e3m2": Format("fp6_e3m2", 6, "minifloat", maxval=28.0),
+    "fp6_e2m3": Format("fp6_e2m3", 6, "minifloat", maxval=7.5),
+    "fp4_e2m1": Format("fp4_e2m1", 4, "minifloat", maxval=6.0),
 }
 # names the reference knows whose quantisation is not on the B200 path (error message, not silence)
-_OTHER = ("f64", "f32", "f16", "bf16", "fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1", "uint8")
+_OTHER = ("f64", "f32", "f16", "bf16", "uint8")
 ALIASES = {"fp64": "f64", "fp32": "f32", "fp16": "f16", "fp8": "fp8_e4m3", "bf8": "fp8_e5m2",
            "e4m3": "fp8_e4m3", "e5m2": "fp8_e5m2", "fp6": "fp6_e3m2", "fp4": "fp4_e2m1",
            "int4_g128": "int4", "w4g128": "int4", "w8": "int8"}
@@ -62,7 +68,7 @@ def get_format(f):
     if name in FORMATS:
         return FORMATS[name]
     if name in _OTHER:
-        raise RuntimeErr(f"numeric format '{name}' is not on the B200 low-bit path (int8, int4)")
+        raise RuntimeErr(f"numeric format '{name}' is not on the B200 low-bit path (int8, int4, fp8, fp6, fp4)")
     raise RuntimeErr(f"unknown numeric format '{name}'; choose one of {', '.join(FORMATS)}")
 
 
@@ -102,6 +108,8 @@ class QTensor:
 
     @property
     def kernel_format(self):
+        if self.fmt.kind == "minifloat":
+            return MINIFLOAT_FMT[self.fmt.name]
         return FMT_INT4_G128 if self.fmt.bits == 4 else FMT_INT8_ROW
 
     def device_tensors(self, device=None):
@@ -110,6 +118,14 @@ class QTensor:
         if _is_torch(self.codes) and self.codes.is_cuda:
             return self.codes, self.scale16
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.fmt.kind == "minifloat":
+            if self._dev is None or self._dev[0] != dev:
+                codes = torch.from_numpy(np.ascontiguousarray(self.codes).view(np.uint8).reshape(-1)).to(dev)
+                sc = self.scale
+                if not isinstance(sc, float):
+                    sc = torch.from_numpy(np.ascontiguousarray(sc, np.float32).reshape(-1)).to(dev)
+                self._dev = (dev, codes, sc)
+            return self._dev[1], self._dev[2]
         if self._dev is None or self._dev[0] != dev:
             R, C = self.rows
             ncols = C // 2 if self.fmt.bits == 4 else C
@@ -168,6 +184,8 @@ def quantize(x, fmt, scale="auto", axis=None, group=None):
     f = get_format(fmt)
     if scale != "auto":
         raise RuntimeErr("the B200 path quantises with scale='auto' (absmax) only")
+    if f.kind == "minifloat":
+        return _quantize_minifloat(x, f, axis)
     if getattr(x, "ndim", np.ndim(x)) != 2 or axis not in (0, -2):
         raise RuntimeErr("the B200 path quantises 2-D arrays with axis=0 (one scale per row, or per row group)")
     R, C = (int(s) for s in x.shape)
@@ -200,6 +218,40 @@ def quantize(x, fmt, scale="auto", axis=None, group=None):
     return QTensor(codes, s32, f, (R, C), axis, None, f.bits == 4, scale16=s16, group=group)
 
 
+def _quantize_minifloat(x, f, axis):
+    """Minifloat quantisation on the device (apsi/precision.py:205-246): axis=0 of a 2-D array (one float32
+    scale per row, shaped [R, 1] as the reference returns it) or axis=None (one float64 scale for the tensor)."""
+    if axis is None:
+        shape = tuple(int(s) for s in np.shape(x))
+        n = int(np.prod(shape)) if shape else 1
+        if n == 0:
+            raise RuntimeErr("cannot quantise an empty array")
+        flat = x.reshape(1, n) if _is_torch(x) else np.asarray(x).reshape(1, n)
+        w, was_np = _to_device_weight(flat)
+    else:
+        if getattr(x, "ndim", np.ndim(x)) != 2 or axis not in (0, -2):
+            raise RuntimeErr("the B200 path quantises minifloats per tensor (axis=None) or per row of a 2-D array "
+                             "(axis=0)")
+        shape = tuple(int(s) for s in x.shape)
+        w, was_np = _to_device_weight(x)
+    R, C = (int(s) for s in w.shape)
+    fmt_id = MINIFLOAT_FMT[f.name]
+    codes, aux = _k.quant_minifloat(w, fmt_id, per_row=axis is not None)
+    if axis is None:
+        m = float(aux.cpu().numpy()[0])
+        scale = m / f.max if (m > 0 and not math.isnan(m)) else 1.0      # the reference's float64 scale
+    else:
+        scale = aux.reshape(R, 1)
+    if was_np:
+        codes = codes.cpu().numpy()
+        if axis is not None:
+            scale = scale.cpu().numpy()
+    packed = f.bits in (4, 6)
+    if f.bits == 8:
+        codes = codes.reshape(shape)
+    return QTensor(codes, scale, f, shape, axis, None, packed)
+
+
 def quantize_linear(W, fmt="int4", group=128):
     """An Apsi Linear weight ``W[in, out]`` quantised for the fused kernels: rows are the outputs, the scales run
     along the inputs (int8: one per output; int4: one per 128 inputs).  ``x @ q`` computes ``x @ W``.
@@ -225,6 +277,14 @@ def dequantize(q):
     if not isinstance(q, QTensor):
         return q
     import torch
+    if q.fmt.kind == "minifloat":
+        on_host = not _is_torch(q.codes)
+        codes, sc = q.device_tensors()
+        n = int(np.prod(q.shape)) if q.shape else 1
+        R, C = (q.shape[0], n // q.shape[0]) if (q.axis is not None and q.shape) else (1, n)
+        out = _k.dequant_minifloat(MINIFLOAT_FMT[q.fmt.name], codes.reshape(-1), R, C,
+                                   sc.reshape(-1) if not isinstance(sc, float) else sc)
+        return out.cpu().numpy().reshape(q.shape) if on_host else out.reshape(q.shape)
     R, C = q.rows
     fmt = q.kernel_format
     on_host = not _is_torch(q.codes)

@@ -17,6 +17,10 @@
  *              two's complement)
  *   Q8_0_G32   words uint32 [N, K/4] (byte j of a word = value j); scale32 float [N, K/32]
  *   Q4_0_G32   words uint32 [N, K/8] (nibble j of a word = value j + 8); scale32 float [N, K/32]
+ *   FP8_E4M3, FP8_E5M2, FP6_E3M2, FP6_E2M3, FP4_E2M1  minifloat codes (sign, exponent, mantissa; the
+ *              reference's value tables), flat row-major: one byte per value (fp8), four values per three
+ *              bytes (fp6, little-endian 24-bit word), two per byte (fp4, even index in the low nibble);
+ *              scale32 float [R] per row, or one tensor scale
  *
  * Arguments are checked before anything is launched; a rejected call leaves the device untouched.
  * There is no CPU fallback: without an sm_100 device every compute call fails with LB_E_DEVICE.
@@ -47,6 +51,11 @@ extern "C" {
 #define LB_FMT_INT4_G128 2
 #define LB_FMT_Q8_0_G32 3
 #define LB_FMT_Q4_0_G32 4
+#define LB_FMT_FP8_E4M3 5 /* minifloats: apsi/precision.py:70-76 (OCP fp8 / MX fp6, fp4 element formats) */
+#define LB_FMT_FP8_E5M2 6
+#define LB_FMT_FP6_E3M2 7
+#define LB_FMT_FP6_E2M3 8
+#define LB_FMT_FP4_E2M1 9
 
 /* element types of weight inputs / dequantised outputs */
 #define LB_DT_F32 0
@@ -115,6 +124,27 @@ int lb_round_g32(int fmt, const void* w, int w_dtype, int64_t N, int64_t K, floa
  * (apsi/precision.py:249-274) and Runner._deq / the deq4, deq8 kernels (apsi/hub_gpu.py:918-950, 1483-1489). */
 int lb_dequant(int fmt, const void* codes, const void* scales, int scale_dtype, int64_t N, int64_t K, void* out,
                int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- minifloats */
+
+/* Bytes of the packed codes of n values in minifloat format fmt (-1 for other formats). */
+int64_t lb_minifloat_bytes(int fmt, int64_t n);
+
+/* Minifloat quantisation of R x C values w (LB_DT_F32 / LB_DT_BF16, row-major): precision.quantize(x, fmt,
+ * scale="auto", axis=0 | None) (apsi/precision.py:205-246, with _minifloat_encode 109-130 and _pack4 / _pack6
+ * 168-192).  per_row != 0 (axis=0): scale32[r] = float32(max|row r| / fmt.max), 1.0 when that maximum is 0 or
+ * NaN, and the values of row r are divided by it.  per_row == 0 (axis=None): absmax[0] receives max|x| over the
+ * tensor (NaN when any value is NaN) and the values are divided by the float64 scale absmax / fmt.max (1.0 when
+ * 0 or NaN), as the reference does with its Python-float scale.  Codes: round to nearest on the grid, ties to
+ * the even code, saturation at +-fmt.max, sign of -0.0 kept, NaN to the format's NaN code; packed flat
+ * (lb_minifloat_bytes(fmt, R*C) bytes).  codes 8-byte aligned. */
+int lb_quant_minifloat(int fmt, const void* w, int w_dtype, int64_t R, int64_t C, int per_row, uint8_t* codes,
+                       float* scale32, float* absmax, void* stream);
+
+/* out[r, c] = value(code) * scale (one float32 multiply; LB_DT_F32 or LB_DT_BF16 out), scale = scale32[r]
+ * (per_row != 0) or tensor_scale: precision.dequantize of a minifloat QTensor (apsi/precision.py:249-274). */
+int lb_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, int per_row, const float* scale32,
+                         float tensor_scale, void* out, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- norm */
 

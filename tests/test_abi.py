@@ -13,7 +13,7 @@ HEADER = os.path.join(build.ROOT, "include", "apsi_lowbit.h")
 
 def declared():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(lb_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(lb_\w+)\s*\(", text, flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -40,7 +40,8 @@ def test_constants_match_header():
     text = open(HEADER).read()
     for name, val in (("LB_E_ARG", _lib.LB_E_ARG), ("LB_E_UNSUPPORTED", _lib.LB_E_UNSUPPORTED),
                       ("LB_FMT_INT4_G128", _lib.FMT_INT4_G128), ("LB_FMT_INT8_ROW", _lib.FMT_INT8_ROW),
-                      ("LB_DT_F16", _lib.DT_F16)):
+                      ("LB_DT_F16", _lib.DT_F16), ("LB_FMT_FP8_E4M3", _lib.FMT_FP8_E4M3),
+                      ("LB_FMT_FP4_E2M1", _lib.FMT_FP4_E2M1)):
         m = re.search(rf"#define {name} \(?(-?\d+)\)?", text)
         assert int(m.group(1)) == val, name
 
@@ -60,6 +61,13 @@ def test_bad_arguments_are_rejected_before_launch(lib):
     assert lib.lb_linear(2, odd, 1, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ALIGN
     assert lib.lb_dequant(2, fake, fake, 5, 4, 128, fake, 0, null) == _lib.LB_E_ARG             # scale dtype
     assert lib.lb_dequant(3, fake, fake, _lib.DT_F16, 4, 128, fake, 0, null) == _lib.LB_E_ARG    # g32 needs f32
+    assert lib.lb_quant_minifloat(2, fake, 0, 4, 8, 1, fake, fake, null, null) == _lib.LB_E_ARG  # not a minifloat
+    assert lib.lb_quant_minifloat(5, fake, 0, 4, 8, 1, fake, null, null, null) == _lib.LB_E_ARG  # per row: scale32
+    assert lib.lb_quant_minifloat(5, fake, 0, 4, 8, 0, fake, null, null, null) == _lib.LB_E_ARG  # tensor: absmax
+    assert lib.lb_quant_minifloat(5, odd, 0, 4, 8, 1, fake, fake, null, null) == _lib.LB_E_ALIGN
+    assert lib.lb_dequant_minifloat(5, fake, 4, 8, 1, null, 1.0, fake, 0, null) == _lib.LB_E_ARG
+    assert lib.lb_dequant_minifloat(9, fake, 4, 8, 0, null, 1.0, fake, 7, null) == _lib.LB_E_ARG  # out dtype
+    assert [lib.lb_minifloat_bytes(f, 7) for f in (5, 6, 7, 8, 9, 2)] == [7, 7, 6, 6, 4, -1]
 
 
 def test_workspace_query(lib):

@@ -1,0 +1,80 @@
+"""Minifloat formats on the GPU (fp8 e4m3 / e5m2, fp6 e3m2 / e2m3, fp4 e2m1): codes, scales and dequantised
+values bit-exact with the reference's golden vectors (precision.quantize / dequantize) and with the oracle."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+NAMES = ("fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1")
+
+
+def _same_f32(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return a.shape == b.shape and np.array_equal(na, nb) and np.array_equal(a.view(np.uint32)[~na],
+                                                                              b.view(np.uint32)[~nb])
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_rows_bit_exact_with_reference_golden(cuda, golden, name):
+    """axis=0: ties to the even code, saturation, a NaN row (scale 1.0), an inf row, signed zeros."""
+    from apsi_b200 import precision as P
+    W = golden[f"mf_{name}_w"]
+    q = P.quantize(W, name, axis=0)
+    np.testing.assert_array_equal(np.asarray(q.codes).reshape(-1), golden[f"mf_{name}_codes"])
+    np.testing.assert_array_equal(np.asarray(q.scale).reshape(-1), golden[f"mf_{name}_scale"])
+    assert np.asarray(q.scale).shape == (W.shape[0], 1)
+    assert _same_f32(P.dequantize(q), golden[f"mf_{name}_deq"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_tensor_scale_bit_exact_with_reference_golden(cuda, golden, name):
+    """axis=None: one float64 scale; packing runs across rows of an odd-sized array."""
+    from apsi_b200 import precision as P
+    W = golden[f"mf_{name}_t_w"]
+    q = P.quantize(W, name)
+    np.testing.assert_array_equal(np.asarray(q.codes).reshape(-1), golden[f"mf_{name}_t_codes"])
+    assert q.scale == float(golden[f"mf_{name}_t_scale"][0])
+    assert _same_f32(P.dequantize(q), golden[f"mf_{name}_t_deq"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+@pytest.mark.parametrize("shape,std", [((257, 1000), 0.02), ((64, 4096), 1.5), ((3, 7), 100.0)])
+def test_random_matches_oracle(cuda, name, shape, std):
+    import torch
+    from apsi_b200 import kernels as K
+    from apsi_b200._lib import MINIFLOAT_FMT
+    rng = np.random.default_rng(shape[0] + shape[1])
+    w = (rng.standard_normal(shape) * std).astype(np.float32)
+    w.reshape(-1)[::97] = -0.0
+    fmt = MINIFLOAT_FMT[name]
+    wt = torch.from_numpy(w).to(cuda)
+    for per_row in (True, False):
+        codes, aux = K.quant_minifloat(wt, fmt, per_row)
+        ref_codes, ref_s = O.quant_minifloat(w, name, 0 if per_row else None)
+        np.testing.assert_array_equal(codes.cpu().numpy(), ref_codes)
+        if per_row:
+            np.testing.assert_array_equal(aux.cpu().numpy(), ref_s.reshape(-1))
+            sc = aux
+        else:
+            m = float(aux.cpu().numpy()[0])
+            assert m == float(np.max(np.abs(w)))
+            sc = ref_s
+        d = K.dequant_minifloat(fmt, codes, shape[0], shape[1], sc)
+        assert _same_f32(d.cpu().numpy(), O.dequant_minifloat(ref_codes, name, shape, ref_s))
+        db = K.dequant_minifloat(fmt, codes, shape[0], shape[1], sc, out_dtype=torch.bfloat16)
+        np.testing.assert_array_equal(db.float().cpu().numpy(), O.bf16_round(d.cpu().numpy()))
+
+
+def test_bfloat16_input_rounds_like_its_float32_value(cuda):
+    import torch
+    from apsi_b200 import kernels as K
+    from apsi_b200._lib import MINIFLOAT_FMT
+    rng = np.random.default_rng(5)
+    w = torch.from_numpy((rng.standard_normal((33, 260)) * 0.3).astype(np.float32)).to(cuda).to(torch.bfloat16)
+    codes, s = K.quant_minifloat(w, MINIFLOAT_FMT["fp8_e4m3"], True)
+    ref_codes, ref_s = O.quant_minifloat(w.float().cpu().numpy(), "fp8_e4m3", 0)
+    np.testing.assert_array_equal(codes.cpu().numpy(), ref_codes)
+    np.testing.assert_array_equal(s.cpu().numpy(), ref_s.reshape(-1))
