@@ -266,9 +266,14 @@ int lb_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, in
 
 static bool use_gemv(int64_t M) { return M <= 16; }
 
+// formats with a fused product: int8 rows, int4 groups of 128, fp8 e4m3 / e5m2 rows (float32 row scales)
+static bool has_product(int fmt) {
+  return fmt == LB_FMT_INT8_ROW || fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP8_E4M3 || fmt == LB_FMT_FP8_E5M2;
+}
+
 int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes) {
   if (!bytes) return fail(LB_E_ARG, "lb_linear_workspace_size: bytes is NULL");
-  if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
+  if (!has_product(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_workspace_size: sizes must be positive");
   *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
@@ -279,7 +284,7 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
                        const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
                        unsigned flags, void* stream, const OutRanks* dst) {
-  if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128)
+  if (!has_product(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (flags & ~static_cast<unsigned>(LB_LINEAR_STATIC_WEIGHTS)) return fail(LB_E_ARG, "lb_linear: unknown flags");
   if (!x || !codes || !scales || !y) return fail(LB_E_ARG, "lb_linear: x, codes, scales and y are required");

@@ -171,6 +171,27 @@ __device__ __forceinline__ void deq_int8_f16(const uint4 a, const uint4 b, uint3
   }
 }
 
+// fp8 rows: 32 bytes of one row -> 16 fp16 pairs, exact, in the pairing of deq_int8_f16 (bytes (0, 2), (1, 3)
+// of each word): e4m3 through the hardware conversion, e5m2 as the high byte of an fp16.
+template <int FMT>
+__device__ __forceinline__ void deq_fp8_f16(const uint4 a, const uint4 b, uint32_t (&o)[16]) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (FMT == 5) {
+      uint32_t d0, d1;
+      const uint32_t s0 = prmt(w[i], 0u, 0x0020u), s1 = prmt(w[i], 0u, 0x0031u);
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\t}" : "=r"(d0) : "r"(s0));
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\t}" : "=r"(d1) : "r"(s1));
+      o[2 * i] = d0;
+      o[2 * i + 1] = d1;
+    } else {
+      o[2 * i] = prmt(w[i], 0u, 0x2404u);
+      o[2 * i + 1] = prmt(w[i], 0u, 0x3414u);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------- the GEMM
 // A (the dequantised weights) and B (the activations) both come from shared memory in the 128-byte swizzled
 // K-major layout; the fp32 accumulators live in tensor memory, two of them, so the epilogue of one tile
@@ -328,7 +349,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           const int sw = (rloc >> 1) & 3;
           const uint4 a = lds_v4(rbase + 16 * ((2 * h) ^ sw));
           const uint4 b = lds_v4(rbase + 16 * ((2 * h + 1) ^ sw));
-          deq_int8_f16(a, b, o);
+          if (FMT == 1) deq_int8_f16(a, b, o);
+          else deq_fp8_f16<FMT>(a, b, o);
         }
         // row rloc, 16-byte chunks 4h .. 4h+3 of its 128-byte K row, 128-byte swizzle: chunk ^= row % 8
         const uint32_t abase = smem_u32(as + slot * A_STAGE) + arow;
@@ -359,6 +381,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       tc_fence_after();
       float rs = 1.f, bias = 0.f;
       if (FMT == 1) rs = __half2float(p.s16[rowc]);
+      if (FMT == 5 || FMT == 6) rs = reinterpret_cast<const float*>(p.s16)[rowc];   // fp8 rows: float32 scales
       if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
       const bool row_ok = row < p.N;
 #pragma unroll 1
@@ -520,6 +543,22 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, p, sms, st);
     if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, p, sms, st);
     return launch_gemm_t<2, 256, false>(tx, tw, p, sms, st);
+  }
+  if (fmt == 5 || fmt == 6) {
+    if (p.dst.n) {
+      if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, true>(tx, tw, p, sms, st)
+                                    : (BN == 128 ? launch_gemm_t<5, 128, true>(tx, tw, p, sms, st)
+                                                 : launch_gemm_t<5, 256, true>(tx, tw, p, sms, st));
+      return BN == 64 ? launch_gemm_t<6, 64, true>(tx, tw, p, sms, st)
+                      : (BN == 128 ? launch_gemm_t<6, 128, true>(tx, tw, p, sms, st)
+                                   : launch_gemm_t<6, 256, true>(tx, tw, p, sms, st));
+    }
+    if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, false>(tx, tw, p, sms, st)
+                                  : (BN == 128 ? launch_gemm_t<5, 128, false>(tx, tw, p, sms, st)
+                                               : launch_gemm_t<5, 256, false>(tx, tw, p, sms, st));
+    return BN == 64 ? launch_gemm_t<6, 64, false>(tx, tw, p, sms, st)
+                    : (BN == 128 ? launch_gemm_t<6, 128, false>(tx, tw, p, sms, st)
+                                 : launch_gemm_t<6, 256, false>(tx, tw, p, sms, st));
   }
   if (p.dst.n) {
     if (BN == 64) return launch_gemm_t<1, 64, true>(tx, tw, p, sms, st);

@@ -111,6 +111,24 @@ __device__ __forceinline__ void deq8_word(uint32_t w, uint32_t& q02, uint32_t& q
   q13 = prmt(v, 0x00006464u, 0x5341u);
 }
 
+// fp8 rows: one word (4 codes) -> the fp16 pairs (code 0, code 2), (code 1, code 3), exact.  e4m3 through the
+// hardware conversion, e5m2 as the high byte of an fp16 (the two formats share exponent width and bias).
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t lo16) {
+  uint32_t d;
+  asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\t}" : "=r"(d) : "r"(lo16));
+  return d;
+}
+template <int FMT>
+__device__ __forceinline__ void deq_fp8_word(uint32_t w, uint32_t& q02, uint32_t& q13) {
+  if (FMT == 5) {
+    q02 = cvt_e4m3x2_f16x2(prmt(w, 0u, 0x0020u));
+    q13 = cvt_e4m3x2_f16x2(prmt(w, 0u, 0x0031u));
+  } else {
+    q02 = prmt(w, 0u, 0x2404u);
+    q13 = prmt(w, 0u, 0x3414u);
+  }
+}
+
 // One unit (16 rows x 64 bytes of codes) against the B fragments of MT token tiles: acc += scale * (sum of
 // exact code products).  `nc` holds minus the offset correction of the thread's two tokens per tile.
 template <int FMT, int MT>
@@ -143,8 +161,13 @@ __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint32_t a[4];
-      deq8_word(W0[i], a[0], a[2]);
-      deq8_word(W8[i], a[1], a[3]);
+      if (FMT == 1) {
+        deq8_word(W0[i], a[0], a[2]);
+        deq8_word(W8[i], a[1], a[3]);
+      } else {
+        deq_fp8_word<FMT>(W0[i], a[0], a[2]);
+        deq_fp8_word<FMT>(W8[i], a[1], a[3]);
+      }
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
         if (i & 1) mma_f16_16816(c1[t], a, B[t][2 * i], B[t][2 * i + 1]);
@@ -202,6 +225,7 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 template <int FMT>
 __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int tok, float v) {
   if (FMT == 1) v *= __half2float(p.s16[n]);
+  if (FMT == 5 || FMT == 6) v *= reinterpret_cast<const float*>(p.s16)[n];   // fp8 rows: float32 scales
   if (p.bias) v += bf16_bits_to_f32(p.bias[n]);
   if (p.dst.n) {                            // this rank's column of every rank's output
     const uint16_t b = f32_to_bf16_bits(v);
@@ -426,7 +450,8 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
             so += __shfl_xor_sync(0xffffffffu, so, o2);
           }
           if (valid && (jj % CPU) == 0)
-            corr[t * units_staged + il * RANGE_UNITS + jj / CPU] = (FMT == 2) ? fmaf(1032.f, se, 72.f * so) : 1152.f * se;
+            corr[t * units_staged + il * RANGE_UNITS + jj / CPU] =
+                (FMT == 2) ? fmaf(1032.f, se, 72.f * so) : (FMT == 1 ? 1152.f * se : 0.f);   // fp8: no offset
         }
         named_sync(1, CT);
       }
@@ -667,6 +692,12 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   if (fmt == 2)
     return M <= 8 ? launch_gemv_t<2, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                   : launch_gemv_t<2, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
+  if (fmt == 5)
+    return M <= 8 ? launch_gemv_t<5, 1, 3, 1>(p, sms, 1, 6, pdl, st)
+                  : launch_gemv_t<5, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
+  if (fmt == 6)
+    return M <= 8 ? launch_gemv_t<6, 1, 3, 1>(p, sms, 1, 6, pdl, st)
+                  : launch_gemv_t<6, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
   return M <= 8 ? launch_gemv_t<1, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                 : launch_gemv_t<1, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
 }

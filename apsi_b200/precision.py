@@ -329,6 +329,14 @@ def qmatmul(a, b, out=None):
     if x2.dtype != torch.bfloat16:
         x2 = x2.to(torch.bfloat16)
     x2 = x2.to(dev, non_blocking=True).contiguous()
+    if b.fmt.kind == "minifloat":
+        y = _minifloat_product(x2, b, R, C, dev, out if not host else None)
+        if y is out and out is not None:
+            return out
+        y = y.reshape(*lead, R)
+        if host:
+            y = y.to("cpu")
+        return y.float().numpy() if was_np else y
     codes, s16 = b.device_tensors(dev)
     if out is not None and not host:
         _k.linear(b.kernel_format, x2, codes, s16, R, out=out.view(-1, R))
@@ -339,6 +347,33 @@ def qmatmul(a, b, out=None):
         y = y.to("cpu")
     if was_np:
         return y.float().numpy()
+    return y
+
+
+def _minifloat_product(x2, b, R, C, dev, out):
+    """x2 [M, C] bfloat16 @ W^T for a minifloat weight W [R, C].  fp8 e4m3 / e5m2: the fused kernels (codes to
+    exact fp16, float32 row scales; a tensor scale is broadcast to the rows).  fp6 / fp4: the library's
+    dequantisation to float32 on the device, then a float32 library GEMM (the reference's own qmatmul order,
+    apsi/precision.py:294-299)."""
+    import torch
+    from ._lib import FMT_FP8_E4M3, FMT_FP8_E5M2
+    fmt_id = b.kernel_format
+    codes, sc = b.device_tensors(dev)
+    if fmt_id in (FMT_FP8_E4M3, FMT_FP8_E5M2):
+        if isinstance(sc, float):
+            s32 = torch.full((R,), float(np.float32(sc)), dtype=torch.float32, device=dev)
+        else:
+            s32 = sc.reshape(-1)
+        if out is not None:
+            _k.linear(fmt_id, x2, codes, s32, R, out=out.view(-1, R))
+            return out
+        return _k.linear(fmt_id, x2, codes, s32, R)
+    w = _k.dequant_minifloat(fmt_id, codes.reshape(-1), *((R, C) if not isinstance(sc, float) else (1, R * C)),
+                             sc.reshape(-1) if not isinstance(sc, float) else sc).reshape(R, C)
+    y = (x2.float() @ w.t()).to(torch.bfloat16)
+    if out is not None:
+        out.view(-1, R).copy_(y)
+        return out
     return y
 
 

@@ -78,3 +78,42 @@ def test_bfloat16_input_rounds_like_its_float32_value(cuda):
     ref_codes, ref_s = O.quant_minifloat(w.float().cpu().numpy(), "fp8_e4m3", 0)
     np.testing.assert_array_equal(codes.cpu().numpy(), ref_codes)
     np.testing.assert_array_equal(s.cpu().numpy(), ref_s.reshape(-1))
+
+
+@pytest.mark.parametrize("name", ["fp8_e4m3", "fp8_e5m2"])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (5, 300, 1024), (16, 520, 2048), (64, 1000, 512),
+                                   (300, 768, 1024)])
+def test_fp8_fused_product_matches_oracle(cuda, name, M, N, K):
+    """Per-row fp8 weights through lb_linear (decode GEMV for M <= 16, tcgen05 GEMM above), against the
+    float64 product of the oracle's dequantised weights: max-abs <= 1e-2 * max|y|, rel. Frobenius <= 2e-3."""
+    import torch
+    from apsi_b200 import precision as P
+    rng = np.random.default_rng(M * 131 + N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = P.quantize(W, name, axis=0)
+    codes, s = O.quant_minifloat(W, name, 0)
+    Wd = O.dequant_minifloat(codes, name, (N, K), s).astype(np.float64)
+    xb = O.bf16_round(x)
+    ref = xb.astype(np.float64) @ Wd.T
+    y = P.qmatmul(torch.from_numpy(xb).to(cuda).to(torch.bfloat16), q).float().cpu().numpy()
+    assert O.max_abs_ratio(y, ref) <= 1e-2
+    assert O.rel_frobenius(y, ref) <= 2e-3
+
+
+@pytest.mark.parametrize("name", ["fp8_e4m3", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1"])
+def test_tensor_scaled_and_packed_products(cuda, name):
+    """axis=None weights and the fp6 / fp4 formats: same tolerance against the oracle's product."""
+    import torch
+    from apsi_b200 import precision as P
+    rng = np.random.default_rng(17)
+    N, K, M = 200, 384, 3
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    x = O.bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    for axis in (0, None):
+        q = P.quantize(W, name, axis=axis)
+        codes, s = O.quant_minifloat(W, name, axis)
+        ref = x.astype(np.float64) @ O.dequant_minifloat(codes, name, (N, K), s).astype(np.float64).T
+        y = P.qmatmul(torch.from_numpy(x).to(cuda).to(torch.bfloat16), q).float().cpu().numpy()
+        assert O.max_abs_ratio(y, ref) <= 1e-2, axis
+        assert O.rel_frobenius(y, ref) <= 2e-3, axis
