@@ -42,6 +42,8 @@ SIGNATURES = [
     ("lb_minifloat_bytes", _I64, [_I, _I64]),
     ("lb_quant_minifloat", _I, [_I, _P, _I, _I64, _I64, _I, _P, _P, _P, _P]),
     ("lb_dequant_minifloat", _I, [_I, _P, _I64, _I64, _I, _P, ctypes.c_float, _P, _I, _P]),
+    ("lb_gguf_encode", _I, [_I, _P, _I64, _P, _P]),
+    ("lb_gguf_decode", _I, [_I, _P, _I64, _P, _P]),
     ("lb_linear_workspace_size", _I, [_I, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     ("lb_linear", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, _P]),
     ("lb_linear_ex", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, ctypes.c_uint, _P]),

@@ -264,6 +264,28 @@ int lb_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, in
                   "dequant_minifloat");
 }
 
+int lb_gguf_encode(int kind, const float* x, int64_t n, uint8_t* blocks, void* stream) {
+  if (kind != 8 && kind != 4) return fail(LB_E_ARG, "lb_gguf_encode: kind must be 8 (Q8_0) or 4 (Q4_0)");
+  if (!x || !blocks) return fail(LB_E_ARG, "lb_gguf_encode: NULL pointer");
+  if (n <= 0 || n % 32) return fail(LB_E_ARG, "lb_gguf_encode: n (%lld) must be a positive multiple of 32", (long long)n);
+  if (!aligned(x, 4)) return fail(LB_E_ALIGN, "lb_gguf_encode: x must be 4-byte aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_gguf(1, kind, x, n, blocks, d->sms, static_cast<cudaStream_t>(stream)), "gguf_encode");
+}
+
+int lb_gguf_decode(int kind, const uint8_t* blocks, int64_t n, float* out, void* stream) {
+  if (kind != 8 && kind != 4) return fail(LB_E_ARG, "lb_gguf_decode: kind must be 8 (Q8_0) or 4 (Q4_0)");
+  if (!blocks || !out) return fail(LB_E_ARG, "lb_gguf_decode: NULL pointer");
+  if (n <= 0 || n % 32) return fail(LB_E_ARG, "lb_gguf_decode: n (%lld) must be a positive multiple of 32", (long long)n);
+  if (!aligned(out, 4)) return fail(LB_E_ALIGN, "lb_gguf_decode: out must be 4-byte aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  return launched(launch_gguf(0, kind, blocks, n, out, d->sms, static_cast<cudaStream_t>(stream)), "gguf_decode");
+}
+
 static bool use_gemv(int64_t M) { return M <= 16; }
 
 // formats with a fused product: int8 rows, int4 groups of 128, fp8 e4m3 / e5m2 rows (float32 row scales)

@@ -45,6 +45,8 @@ cudaError_t launch_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, i
                                      const float* scale32, float tscale, void* out, int out_dt, int sms,
                                      cudaStream_t st);
 
+cudaError_t launch_gguf(int encode, int kind, const void* src, int64_t n, void* dst, int sms, cudaStream_t st);
+
 cudaError_t launch_interleave(const void* src, int G, int64_t M, int64_t Nl, void* dst, int sms, cudaStream_t st);
 
 }  // namespace lb

@@ -13,7 +13,8 @@ from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F3
 
 __all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "round_g32", "dequant", "linear",
            "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
-           "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError", "minifloat_bytes", "quant_minifloat", "dequant_minifloat"]
+           "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError", "minifloat_bytes", "quant_minifloat", "dequant_minifloat",
+           "gguf_encode", "gguf_decode"]
 
 
 def _ptr(t):
@@ -133,6 +134,28 @@ def dequant_minifloat(fmt, codes, R, C, scale, out_dtype=torch.float32):
         _lib.call("lb_dequant_minifloat", fmt, _ptr(codes), R, C, 1 if per_row else 0,
                   _ptr(scale) if per_row else ctypes.c_void_p(0), ctypes.c_float(0.0 if per_row else float(scale)),
                   _ptr(out), dt, _stream(codes.device))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ GGUF
+def gguf_encode(x, kind):
+    """GGUF Q8_0 (kind 8) or Q4_0 (kind 4) block bytes of a float32 CUDA tensor (size a multiple of 32)."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float32:
+        raise LowbitError(_lib.LB_E_ARG, f"x must be float32, got {x.dtype}")
+    n = x.numel()
+    out = torch.empty(((n // 32) * (34 if kind == 8 else 18),), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("lb_gguf_encode", kind, _ptr(x), n, _ptr(out), _stream(x.device))
+    return out
+
+
+def gguf_decode(blocks, kind, n):
+    """float32 values [n] of GGUF Q8_0 / Q4_0 blocks (a uint8 CUDA tensor)."""
+    _need_cuda(blocks, "blocks")
+    out = torch.empty((n,), dtype=torch.float32, device=blocks.device)
+    with torch.cuda.device(blocks.device):
+        _lib.call("lb_gguf_decode", kind, _ptr(blocks), n, _ptr(out), _stream(blocks.device))
     return out
 
 

@@ -30,9 +30,10 @@ import struct
 
 import numpy as np
 
+from . import kernels as _k
 from .precision import QTensor, get_format, RuntimeErr
 
-__all__ = ["save_packed", "load_packed", "as_linear", "FORMAT", "VERSION"]
+__all__ = ["save_packed", "load_packed", "as_linear", "FORMAT", "VERSION", "gguf_q8_0", "gguf_q4_0", "gguf_dequant"]
 
 FORMAT = "apsi-model"          # the reference's container tag (apsi/modelio.py:30-31)
 VERSION = "1"
@@ -242,3 +243,49 @@ def as_linear(q, rows):
     scale = np.asarray(q.scale, np.float32).reshape(rows, C // 128)
     s16 = np.asarray(q.scale16).reshape(rows, C // 128)
     return QTensor(q.codes, scale, q.fmt, (rows, C), 0, None, True, scale16=s16, group=128)
+
+
+# ------------------------------------------------------------------------------------------------ GGUF blocks
+def _gguf_device_input(a):
+    import torch
+    if isinstance(a, torch.Tensor):
+        t = a.detach().reshape(-1)
+        was_np = False
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32).reshape(-1)))
+        was_np = True
+    if not t.is_cuda:
+        t = t.to(torch.device("cuda", torch.cuda.current_device()))
+    return t.to(torch.float32).contiguous(), was_np
+
+
+def gguf_q8_0(a):
+    """GGUF Q8_0 block bytes of a float array (size a multiple of 32), computed on the GPU: the bytes of the
+    reference's ``modelio._q8_0`` (apsi/modelio.py:56-67).  NumPy in -> ``bytes`` out; CUDA tensor in -> uint8
+    CUDA tensor out."""
+    t, was_np = _gguf_device_input(a)
+    out = _k.gguf_encode(t, 8)
+    return out.cpu().numpy().tobytes() if was_np else out
+
+
+def gguf_q4_0(a):
+    """GGUF Q4_0 block bytes (apsi/modelio.py:70-81, ``modelio._q4_0``), computed on the GPU."""
+    t, was_np = _gguf_device_input(a)
+    out = _k.gguf_encode(t, 4)
+    return out.cpu().numpy().tobytes() if was_np else out
+
+
+def gguf_dequant(buf, kind, n):
+    """float32 values of Q8_0 (kind "q8_0") or Q4_0 ("q4_0") blocks (apsi/modelio.py:84-95), on the GPU."""
+    import torch
+    if isinstance(buf, torch.Tensor):
+        b, was_np = buf.reshape(-1).contiguous(), False
+        if not b.is_cuda:
+            b, was_np = b.to(torch.device("cuda", torch.cuda.current_device())), True
+    else:
+        b = torch.from_numpy(np.frombuffer(bytes(buf), np.uint8).copy()).to(
+            torch.device("cuda", torch.cuda.current_device()))
+        was_np = True
+    nb = (n + 31) // 32 * 32
+    out = _k.gguf_decode(b, 8 if kind == "q8_0" else 4, nb)[:n]
+    return out.cpu().numpy() if was_np else out

@@ -146,6 +146,18 @@ int lb_quant_minifloat(int fmt, const void* w, int w_dtype, int64_t R, int64_t C
 int lb_dequant_minifloat(int fmt, const uint8_t* codes, int64_t R, int64_t C, int per_row, const float* scale32,
                          float tensor_scale, void* out, int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- GGUF */
+
+/* GGUF blocks of 32 float32 values (n a multiple of 32): kind 8 = Q8_0 (34 bytes per block: binary16
+ * d = amax / 127, 32 int8 codes sign(y) * floor(|y| + 0.5) of y = x / d), kind 4 = Q4_0 (18 bytes per block:
+ * binary16 d = x[first argmax |x|] / -8, codes min(15, trunc(x / d + 8.5)), value j in the low and value j + 16
+ * in the high nibble of byte j); float32 arithmetic as the reference's writer.  Replaces the GGUF codec of
+ * modelio.save_gguf (apsi/modelio.py:56-81, _q8_0 / _q4_0); finite inputs. */
+int lb_gguf_encode(int kind, const float* x, int64_t n, uint8_t* blocks, void* stream);
+
+/* float32 values d * code of GGUF Q8_0 / Q4_0 blocks (apsi/modelio.py:84-95, _dq8_0 / _dq4_0). */
+int lb_gguf_decode(int kind, const uint8_t* blocks, int64_t n, float* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- norm */
 
 /* RMSNorm of activation rows, the prologue of a normalised projection: out[m, k] = bf16(x[m, k] *
@@ -184,7 +196,9 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
  * per group in float32; needs no workspace); larger M runs the tcgen05 GEMM (fp16 operands, x rescaled per
  * row by a power of two, float32 accumulation in tensor memory), whose converted activations live in
  * `workspace` (lb_linear_workspace_size() bytes, 256-byte aligned, contents need no initialisation).
- * x, codes and scales must be 16-byte aligned.
+ * x, codes and scales must be 16-byte aligned.  Formats: INT8_ROW and INT4_G128 (binary16 scales), FP8_E4M3
+ * and FP8_E5M2 rows (codes uint8 [N, K], float32 scales [N]: the codes become exact fp16 operands); the other
+ * formats return LB_E_UNSUPPORTED.
  * Replaces precision.qmatmul / models.qlinear (apsi/precision.py:294-299, apsi/models.py:302-308) and
  * _Base.linear -> Runner.gemv / Runner.gemm with bias and acc (apsi/hub_gpu.py:1305-1315, 1491-1528). */
 int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
