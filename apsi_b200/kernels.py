@@ -14,7 +14,7 @@ from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F3
 __all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "round_g32", "dequant", "linear",
            "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
            "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError", "minifloat_bytes", "quant_minifloat", "dequant_minifloat",
-           "gguf_encode", "gguf_decode"]
+           "gguf_encode", "gguf_decode", "linear_spec"]
 
 
 def _ptr(t):
@@ -241,6 +241,36 @@ def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False, stat
     finally:
         if switch:
             torch.cuda.set_device(prev)
+    if rc:
+        _lib.check(rc)
+    return out
+
+
+try:                                                   # raw current stream / device of torch, without objects
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+    _cur_dev = torch._C._cuda_getDevice
+except AttributeError:                                 # pragma: no cover
+    _raw_stream = None
+    _cur_dev = None
+
+
+def linear_spec(spec, x, out=None):
+    """``linear`` for a weight described by ``spec`` = (fmt, codes pointer, scales pointer, N, K, device index)
+    and a contiguous bfloat16 CUDA x [M, K] on the current device, in the fewest host operations: the per-call
+    path of ``precision.qmatmul``.  Returns None (the caller takes the general path) when x, out or the device
+    do not fit it."""
+    fmt, cptr, sptr, N, K, dev = spec
+    if _raw_stream is None or x.shape[1] != K or not x.is_contiguous() or x.get_device() != dev or _cur_dev() != dev:
+        return None
+    M = x.shape[0]
+    if M > 16:
+        return None                                     # the prefill path needs a workspace: general path
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    elif out.dim() != 2 or out.shape[0] != M or out.shape[1] != N or out.stride(1) != 1 or out.dtype != x.dtype:
+        return None
+    rc = _fn("lb_linear_ex")(fmt, x.data_ptr(), M, K, cptr, sptr, N, None, 0, out.data_ptr(), out.stride(0), None,
+                             0, 0, _raw_stream(dev))
     if rc:
         _lib.check(rc)
     return out

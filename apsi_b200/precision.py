@@ -80,13 +80,30 @@ class QTensor:
     and float32 scales shaped as the reference returns them).  B200 additions: ``scale16`` (the binary16
     scales the kernels read), ``group`` (128 for int4 groups, None for one scale per row), ``kn`` (True when
     the logical array is ``[in, out]`` and the rows stored are its transpose, see ``quantize_linear``)."""
-    __slots__ = ("codes", "scale", "fmt", "shape", "axis", "dim", "packed", "scale16", "group", "kn", "_dev")
+    __slots__ = ("codes", "scale", "fmt", "shape", "axis", "dim", "packed", "scale16", "group", "kn", "_dev",
+                 "_fast")
 
     def __init__(self, codes, scale, fmt, shape, axis, dim=None, packed=False, scale16=None, group=None, kn=False):
         self.codes, self.scale, self.fmt, self.shape = codes, scale, fmt, tuple(shape)
         self.axis, self.dim, self.packed = axis, dim, packed
         self.scale16, self.group, self.kn = scale16, group, kn
         self._dev = None
+        self._fast = None
+
+    def fast_spec(self):
+        """(fmt, codes pointer, scales pointer, N, K, device index) for the per-call fast path of ``qmatmul``, or
+        None when the operand does not qualify (host codes, minifloat formats).  Rebuilt when ``codes`` or
+        ``scale16`` are replaced."""
+        c, s16 = self.codes, self.scale16
+        f = self._fast
+        if f is not None and f[0] is c and f[1] is s16:
+            return f[2]
+        spec = None
+        if self.fmt.kind == "int" and _is_torch(c) and c.is_cuda and s16 is not None and s16.is_cuda:
+            R, C = self.rows
+            spec = (self.kernel_format, c.data_ptr(), s16.data_ptr(), R, C, c.get_device())
+        self._fast = (c, s16, spec)
+        return spec
 
     @property
     def nbytes(self):
@@ -146,6 +163,17 @@ class QTensor:
     def __repr__(self):
         g = f", g{self.group}" if self.group else ""
         return f"QTensor[{'x'.join(map(str, self.shape))}, {self.fmt.name}{g}, {self.nbytes} bytes]"
+
+
+def _torch_types():
+    try:
+        import torch
+        return (torch.Tensor, torch.bfloat16)
+    except ImportError:                                  # pragma: no cover
+        return (None, None)
+
+
+_TORCH_TENSOR = _torch_types()
 
 
 def _is_torch(a):
@@ -308,6 +336,13 @@ def qmatmul(a, b, out=None):
     a CUDA tensor stays on the device (bfloat16 out); NumPy / CPU inputs are copied in and the result copied
     back as float32 (NumPy) or bfloat16 (torch).  ``out`` (B200 extension): a bfloat16 CUDA tensor ``[..., N]``
     to write into (CUDA inputs only)."""
+    # per-call fast path: a contiguous bfloat16 CUDA matrix times a device int4 / int8 weight
+    if type(b) is QTensor and type(a) is _TORCH_TENSOR[0]:
+        spec = b.fast_spec()
+        if spec is not None and a.dtype is _TORCH_TENSOR[1] and a.dim() == 2 and a.is_cuda:
+            y = _k.linear_spec(spec, a, out)
+            if y is not None:
+                return y
     import torch
     if isinstance(a, QTensor):
         raise RuntimeErr("the B200 path quantises the weight (right) operand only")

@@ -150,3 +150,22 @@ def test_static_weight_overlap_waits_for_the_activations(cuda):
     torch.cuda.synchronize()
     for a, b in zip(ref, outs):
         assert torch.equal(a, b)
+
+
+def test_qmatmul_fast_path_matches_general_path(cuda):
+    """precision.qmatmul's per-call fast path (a contiguous bf16 CUDA matrix, M <= 16) gives the same bits as
+    the general path (a 3-D input), with and without ``out``, and follows a replaced codes tensor."""
+    import torch
+    from apsi_b200 import precision as P
+    rng = np.random.default_rng(44)
+    W = torch.from_numpy((rng.standard_normal((1000, 1024)) * 0.02).astype(np.float32)).to(cuda)
+    q = P.quantize(W, "int4", axis=0, group=128)
+    x = torch.from_numpy(rng.standard_normal((5, 1024)).astype(np.float32)).to(cuda).to(torch.bfloat16)
+    y_fast = P.qmatmul(x, q)
+    y_gen = P.qmatmul(x.unsqueeze(0), q)[0]
+    assert torch.equal(y_fast, y_gen)
+    out = torch.empty((5, 1000), dtype=torch.bfloat16, device=cuda)
+    assert P.qmatmul(x, q, out=out) is out and torch.equal(out, y_gen)
+    q2 = P.quantize(W * 2, "int4", axis=0, group=128)
+    q.codes, q.scale16 = q2.codes, q2.scale16                # replaced tensors: the cached spec is rebuilt
+    assert torch.equal(P.qmatmul(x, q), P.qmatmul(x.unsqueeze(0), q2)[0])
