@@ -21,6 +21,7 @@
 //   warps 10..13  epilogue: tcgen05.ld -> scale / bias / accumulate -> bf16 -> global
 // All mbarrier waits are bounded (lb::mbar_wait); a timeout sets the device error word and the CTA drains.
 #include <cuda.h>
+#include <string.h>
 #include "lb_common.cuh"
 #include "lb_kernels.h"
 
@@ -52,8 +53,28 @@ struct GemmParams {
   int64_t M, N, K, ldy;
   int acc;
   int m_blocks, n_blocks, tiles, ksteps;
+  // Work units.  Units [0, full) are whole BM x BN tiles.  When the last wave of tiles would leave most SMs
+  // idle, tiles full .. tiles - 1 are each cut along the tokens into `parts` units of sbn = BN / parts tokens
+  // (the MMA's N and the activation box shrink; k order and accumulation per output are unchanged).
+  int units, full, parts, sbn;
   OutRanks dst;             // column-sharded layer: every rank's output (dst.n == 0: y)
 };
+
+// unit -> weight row block, first token, tokens
+__device__ __forceinline__ void gemm_unit(const GemmParams& p, int u, int bn, int& mb, int& tok0, int& width) {
+  int tile, part = 0;
+  if (u < p.full) {
+    tile = u;
+  } else {
+    const int s = u - p.full;
+    tile = p.full + s / p.parts;
+    part = s - (s / p.parts) * p.parts;
+  }
+  mb = tile / p.n_blocks;
+  const int nb = tile - mb * p.n_blocks;
+  tok0 = nb * bn + part * p.sbn;
+  width = u < p.full ? bn : p.sbn;
+}
 
 template <int FMT>
 struct GemmCfg {
@@ -210,7 +231,7 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
 template <int FMT, int BN, bool SH>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                const GemmParams p) {
+                const __grid_constant__ CUtensorMap tm_xs, const GemmParams p) {
   using namespace gemm;
   using Cfg = GemmCfg<FMT>;
   using Sm = GemmSmem<BN>;
@@ -249,6 +270,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     fence_barrier_init();
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_w);
+    if (p.parts > 1) prefetch_tmap(&tm_xs);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, Sm::TMEM_COLS);
@@ -264,13 +286,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
-        const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+        int mb, tok0, width;
+        gemm_unit(p, u, BN, mb, tok0, width);
         for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
           const uint32_t slot = it % STAGES;
           if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
-          mbar_arrive_expect_tx(&full_x[slot], Sm::X_STAGE);
-          tma_load_2d(xs + slot * Sm::X_STAGE, &tm_x, ks * BK, nb * BN, &full_x[slot]);
+          mbar_arrive_expect_tx(&full_x[slot], static_cast<uint32_t>(width) * 128u);
+          tma_load_2d(xs + slot * Sm::X_STAGE, width == BN ? &tm_x : &tm_xs, ks * BK, tok0, &full_x[slot]);
           mbar_arrive_expect_tx(&full_w[slot], Cfg::RAW_STAGE);
           tma_load_2d(raw + slot * Cfg::RAW_STAGE, &tm_w, ks * Cfg::RAW_ROW, mb * BM, &full_w[slot]);
         }
@@ -279,9 +302,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
       uint32_t it = 0, tcount = 0;
-      for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
+      for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tcount) {
+        int mb, tok0, width;
+        gemm_unit(p, u, BN, mb, tok0, width);
+        const uint32_t idesc = idesc_f16_f32(BM, width);
         const uint32_t b = tcount & 1;
         if (tcount >= 2) mbar_wait(&acc_empty[b], ((tcount >> 1) - 1) & 1, abort_v);   // epilogue of tile - 2
         tc_fence_after();
@@ -310,8 +335,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const int h = d >> 7;                   // K half of each stage (32 values = 64 bytes of fp16)
     const uint32_t arow = static_cast<uint32_t>((rloc >> 3) * 1024 + (rloc & 7) * 128);
     uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x) {
-      const int mb = tile / p.n_blocks;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+      int mb, tok0, width;
+      gemm_unit(p, u, BN, mb, tok0, width);
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
       // int4 scales of this row, one group of 128 per two stages, fetched four groups ahead through a small
@@ -372,8 +398,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const int rloc = q * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     uint32_t tcount = 0;
-    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++tcount) {
-      const int mb = tile / p.n_blocks, nb = tile % p.n_blocks;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tcount) {
+      int mb, tok0, width;
+      gemm_unit(p, u, BN, mb, tok0, width);
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
       const uint32_t b = tcount & 1;
@@ -385,13 +412,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
       const bool row_ok = row < p.N;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = 0; c0 < width; c0 += 16) {
         uint32_t dv[16];
         tmem_ld_x16(tmem + lane_addr + b * BN + c0, dv);
         tc_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int64_t tok = static_cast<int64_t>(nb) * BN + c0 + j;
+          const int64_t tok = static_cast<int64_t>(tok0) + c0 + j;
           if (row_ok && tok < p.M) {
             float v = __uint_as_float(dv[j]) * (p.tokscale[tok] * rs);
             v += bias;
@@ -452,8 +479,8 @@ size_t gemm_workspace_bytes(int64_t M, int64_t K) {
 }
 
 template <int FMT, int BN, bool SH>
-static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, const GemmParams& p, int sms,
-                                 cudaStream_t st) {
+static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& txs,
+                                 const GemmParams& p, int sms, cudaStream_t st) {
   const size_t smem = gemm_smem_bytes(FMT, BN);
   static thread_local int configured_dev = -1;
   int dev = 0;
@@ -464,8 +491,8 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, c
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
-  const int grid = p.tiles < sms ? p.tiles : sms;
-  gemm_kernel<FMT, BN, SH><<<grid, gemm::THREADS, smem, st>>>(tx, tw, p);
+  const int grid = p.units < sms ? p.units : sms;
+  gemm_kernel<FMT, BN, SH><<<grid, gemm::THREADS, smem, st>>>(tx, tw, txs, p);
   return cudaGetLastError();
 }
 
@@ -492,7 +519,7 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     if (e != cudaSuccess) return e;
   }
   const int BN = gemm_bn_for(M);
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, txs;
   {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
@@ -533,41 +560,73 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   p.n_blocks = static_cast<int>((M + BN - 1) / BN);
   p.tiles = p.m_blocks * p.n_blocks;
   p.ksteps = static_cast<int>(K / gemm::BK);
+  // a last wave under half full: cut its tiles along the tokens so every SM ends at about the same time
+  p.units = p.tiles;
+  p.full = p.tiles;
+  p.parts = 1;
+  p.sbn = BN;
+  {
+    const int rem = p.tiles % sms;
+    if (BN >= 128 && p.tiles > sms && rem > 0 && rem * 2 <= sms) {
+      int parts = BN / 64;
+      while (parts > 1 && rem * parts > sms) parts >>= 1;
+      if (parts > 1) {
+        p.full = p.tiles - rem;
+        p.parts = parts;
+        p.sbn = BN / parts;
+        p.units = p.full + rem * parts;
+      }
+    }
+  }
+  memcpy(&txs, &tx, sizeof(tx));
+  if (p.parts > 1) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(gemm::BK), static_cast<cuuint32_t>(p.sbn)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&txs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      *why = "cuTensorMapEncodeTiled failed for the activation tensor (last-wave box)";
+      return cudaErrorInvalidValue;
+    }
+  }
   p.dst = dst ? *dst : OutRanks{};
   if (fmt == 2) {
     if (p.dst.n) {
-      if (BN == 64) return launch_gemm_t<2, 64, true>(tx, tw, p, sms, st);
-      if (BN == 128) return launch_gemm_t<2, 128, true>(tx, tw, p, sms, st);
-      return launch_gemm_t<2, 256, true>(tx, tw, p, sms, st);
+      if (BN == 64) return launch_gemm_t<2, 64, true>(tx, tw, txs, p, sms, st);
+      if (BN == 128) return launch_gemm_t<2, 128, true>(tx, tw, txs, p, sms, st);
+      return launch_gemm_t<2, 256, true>(tx, tw, txs, p, sms, st);
     }
-    if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, p, sms, st);
-    if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, p, sms, st);
-    return launch_gemm_t<2, 256, false>(tx, tw, p, sms, st);
+    if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, txs, p, sms, st);
+    if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, txs, p, sms, st);
+    return launch_gemm_t<2, 256, false>(tx, tw, txs, p, sms, st);
   }
   if (fmt == 5 || fmt == 6) {
     if (p.dst.n) {
-      if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, true>(tx, tw, p, sms, st)
-                                    : (BN == 128 ? launch_gemm_t<5, 128, true>(tx, tw, p, sms, st)
-                                                 : launch_gemm_t<5, 256, true>(tx, tw, p, sms, st));
-      return BN == 64 ? launch_gemm_t<6, 64, true>(tx, tw, p, sms, st)
-                      : (BN == 128 ? launch_gemm_t<6, 128, true>(tx, tw, p, sms, st)
-                                   : launch_gemm_t<6, 256, true>(tx, tw, p, sms, st));
+      if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, true>(tx, tw, txs, p, sms, st)
+                                    : (BN == 128 ? launch_gemm_t<5, 128, true>(tx, tw, txs, p, sms, st)
+                                                 : launch_gemm_t<5, 256, true>(tx, tw, txs, p, sms, st));
+      return BN == 64 ? launch_gemm_t<6, 64, true>(tx, tw, txs, p, sms, st)
+                      : (BN == 128 ? launch_gemm_t<6, 128, true>(tx, tw, txs, p, sms, st)
+                                   : launch_gemm_t<6, 256, true>(tx, tw, txs, p, sms, st));
     }
-    if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, false>(tx, tw, p, sms, st)
-                                  : (BN == 128 ? launch_gemm_t<5, 128, false>(tx, tw, p, sms, st)
-                                               : launch_gemm_t<5, 256, false>(tx, tw, p, sms, st));
-    return BN == 64 ? launch_gemm_t<6, 64, false>(tx, tw, p, sms, st)
-                    : (BN == 128 ? launch_gemm_t<6, 128, false>(tx, tw, p, sms, st)
-                                 : launch_gemm_t<6, 256, false>(tx, tw, p, sms, st));
+    if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, false>(tx, tw, txs, p, sms, st)
+                                  : (BN == 128 ? launch_gemm_t<5, 128, false>(tx, tw, txs, p, sms, st)
+                                               : launch_gemm_t<5, 256, false>(tx, tw, txs, p, sms, st));
+    return BN == 64 ? launch_gemm_t<6, 64, false>(tx, tw, txs, p, sms, st)
+                    : (BN == 128 ? launch_gemm_t<6, 128, false>(tx, tw, txs, p, sms, st)
+                                 : launch_gemm_t<6, 256, false>(tx, tw, txs, p, sms, st));
   }
   if (p.dst.n) {
-    if (BN == 64) return launch_gemm_t<1, 64, true>(tx, tw, p, sms, st);
-    if (BN == 128) return launch_gemm_t<1, 128, true>(tx, tw, p, sms, st);
-    return launch_gemm_t<1, 256, true>(tx, tw, p, sms, st);
+    if (BN == 64) return launch_gemm_t<1, 64, true>(tx, tw, txs, p, sms, st);
+    if (BN == 128) return launch_gemm_t<1, 128, true>(tx, tw, txs, p, sms, st);
+    return launch_gemm_t<1, 256, true>(tx, tw, txs, p, sms, st);
   }
-  if (BN == 64) return launch_gemm_t<1, 64, false>(tx, tw, p, sms, st);
-  if (BN == 128) return launch_gemm_t<1, 128, false>(tx, tw, p, sms, st);
-  return launch_gemm_t<1, 256, false>(tx, tw, p, sms, st);
+  if (BN == 64) return launch_gemm_t<1, 64, false>(tx, tw, txs, p, sms, st);
+  if (BN == 128) return launch_gemm_t<1, 128, false>(tx, tw, txs, p, sms, st);
+  return launch_gemm_t<1, 256, false>(tx, tw, txs, p, sms, st);
 }
 
 }  // namespace lb

@@ -79,11 +79,12 @@ def test_bias_and_accumulate(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 11008, 4096), (4, 4096, 11008), (1, 8192, 28672), (16, 2048, 4096),
-                                   (2, 1376, 4096), (1, 28672, 8192)])
+                                   (2, 1376, 4096), (1, 28672, 8192), (300, 12288, 1024), (2048, 12288, 4096)])
 @pytest.mark.parametrize("shards", [2, 8])
 def test_column_shards_are_bit_identical(cuda, M, N, K, shards):
     """Each shard of rows computed alone (the multi-GPU layout) gives exactly the full product's columns,
-    even when the shard runs on a different execution path (cluster split vs persistent)."""
+    even when the shard runs on a different execution path (cluster split vs persistent GEMV; whole tiles vs
+    the token-cut tiles of a GEMM's last wave)."""
     import torch
     from apsi_b200 import kernels as Kn
     from apsi_b200._lib import FMT_INT4_G128
