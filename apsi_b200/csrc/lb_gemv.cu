@@ -185,6 +185,53 @@ __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const
   }
 }
 
+// m16n8k32 product of unsigned 8-bit A and signed 8-bit B, int32 accumulate: d += a * b.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (a ^ b) & c
+__device__ __forceinline__ uint32_t lop3_xor_and(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// int4 unit on the integer tensor path: codes as unsigned bytes q + 8 (one LOP3 per four), activations as two
+// signed 8-bit digits of a 2^e-scaled int16 (hi in column 2t, lo in column 2t + 1 of the n8 tile), exact int32
+// products; `nc` starts the accumulation at -8 * sum(digits) (the offset correction), `f` is 2^e of the thread's
+// token.  Output: acc[T][0] (row g) and acc[T][1] (row g + 8) for token 4T + c.
+template <int NT>
+__device__ __forceinline__ void unit_i8(const uint4& w0, const uint4& w8, const uint32_t (&B)[NT][8],
+                                        const int (&nc)[NT][2], const float (&f)[NT], float s0, float s8,
+                                        float (&acc)[NT][2]) {
+  const uint32_t W0[4] = {w0.x, w0.y, w0.z, w0.w};
+  const uint32_t W8[4] = {w8.x, w8.y, w8.z, w8.w};
+  uint32_t A[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    A[i][0] = lop3_xor_and(W0[i], 0x88888888u, 0x0F0F0F0Fu);          // row g, even positions
+    A[i][1] = lop3_xor_and(W8[i], 0x88888888u, 0x0F0F0F0Fu);          // row g + 8
+    A[i][2] = lop3_xor_and(W0[i] >> 4, 0x08080808u, 0x0F0F0F0Fu);     // row g, odd positions
+    A[i][3] = lop3_xor_and(W8[i] >> 4, 0x08080808u, 0x0F0F0F0Fu);
+  }
+#pragma unroll
+  for (int T = 0; T < NT; ++T) {
+    int da[4] = {-nc[T][0], -nc[T][1], -nc[T][0], -nc[T][1]};
+    int db[4] = {0, 0, 0, 0};
+    mma_u8s8(da, A[0], B[T][0], B[T][1]);
+    mma_u8s8(db, A[1], B[T][2], B[T][3]);
+    mma_u8s8(da, A[2], B[T][4], B[T][5]);
+    mma_u8s8(db, A[3], B[T][6], B[T][7]);
+    const int v0 = (da[0] + db[0]) * 256 + (da[1] + db[1]);
+    const int v8 = (da[2] + db[2]) * 256 + (da[3] + db[3]);
+    acc[T][0] = fmaf(static_cast<float>(v0), s0 * f[T], acc[T][0]);
+    acc[T][1] = fmaf(static_cast<float>(v8), s8 * f[T], acc[T][1]);
+  }
+}
+
 // Shared-memory carve-up, in bytes from the base of dynamic shared memory.
 struct GemvSmem {
   int ring, xs, corr, xsc, gred, ptab, zeros, bars, total;
@@ -195,14 +242,14 @@ struct GemvSmem {
 __host__ __device__ inline GemvSmem gemv_smem(int fmt, int M, int MT, int G, int xs_units, int slots, int items) {
   using namespace gemv;
   GemvSmem s;
-  const int xu = (fmt == 2) ? 256 : 128;     // staged bytes of x per unit per token
+  const int xu = (fmt == 2 || fmt == 20) ? 256 : 128;     // staged bytes of x per unit per token
   s.token_stride = xs_units * xu + 64;
   s.ring = 0;
   s.xs = slots * STAGE_BYTES;                                  // multiple of 128
   s.corr = s.xs + ((M * s.token_stride + 127) & ~127);
-  s.xsc = s.corr + ((M * xs_units * 4 + 127) & ~127);
+  s.xsc = s.corr + ((M * xs_units * (fmt == 20 ? 12 : 4) + 127) & ~127);   // int core: int2 + 2^e; else float
   s.gred = s.xsc + 2 * 16 * MAX_RANGES * 4;                    // xsc + xmax
-  s.ptab = s.gred + G * 2 * GW * 32 * 4 * MT * 4;              // double-buffered group partials
+  s.ptab = s.gred + G * 2 * GW * 32 * (fmt == 20 ? 2 : 4) * MT * 4;   // double-buffered group partials
   s.zeros = s.ptab + ((items * 16 * M * 4 + 127) & ~127);
   s.bars = s.zeros + 256;                                      // 256 zero bytes (absent tokens)
   s.total = s.bars + 2 * MAX_SLOTS * 8 + 16;
@@ -245,11 +292,13 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
   using namespace gemv;
   constexpr int NCW = G * GW;                  // consumer warps
   constexpr int CT = NCW * 32;                 // consumer threads
-  constexpr int XU = (FMT == 2) ? 256 : 128;   // staged bytes of x per unit per token
+  constexpr bool I4 = (FMT == 2 || FMT == 20);   // int4 codes (20: on the integer tensor path)
+  constexpr int XU = I4 ? 256 : 128;            // staged bytes of x per unit per token
   constexpr int XCH = XU / 64;                 // 16-byte chunks of x per thread per unit
-  constexpr int KPU = (FMT == 2) ? 128 : 64;   // K values per unit
+  constexpr int KPU = I4 ? 128 : 64;            // K values per unit
   constexpr int CPU = KPU / 8;                 // 16-byte chunks of x per unit
   constexpr int CPR = RANGE_UNITS * CPU;       // 16-byte chunks of x per range
+  constexpr int PW = (FMT == 20) ? 2 : 4;      // partial floats per lane per token tile
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
 
   const int R = p.R;
@@ -279,7 +328,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t row_bytes = (FMT == 2) ? p.K / 2 : p.K;
+  const int64_t row_bytes = I4 ? p.K / 2 : p.K;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < slots; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], GW); }
@@ -335,7 +384,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       };
       auto slot_of = [&](int t, int il, int jj) -> uint8_t* {
         int u, cc, vv;
-        if (FMT == 2) { u = jj >> 4; cc = (jj >> 2) & 3; vv = jj & 3; }
+        if (I4) { u = jj >> 4; cc = (jj >> 2) & 3; vv = jj & 3; }
         else { u = jj >> 3; cc = (jj >> 1) & 3; vv = jj & 1; }
         return xs + t * L.token_stride + (il * RANGE_UNITS + u) * XU + vv * 64 + cc * 16;
       };
@@ -370,6 +419,84 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
 #pragma unroll
             for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o2);
             if (ok && (jj % CPU) == 0) corr[t * units_staged + il * RANGE_UNITS + jj / CPU] = 136.f * sum;
+          }
+        }
+        named_sync(1, CT);
+      } else if (FMT == 20) {
+        // int4 on the integer path: per (token, unit) e with max|x| * 2^-e in [2^13, 2^14), x16 = rint(x * 2^-e), split into signed
+        // bytes hi = (x16 + 128) >> 8 and lo = x16 - 256 hi, written in the B-fragment order of the m16n8k32
+        // tiles (column 2t: hi, 2t + 1: lo of token t); the offset correction 8 * sum(digit) per (token, unit)
+        int* corr_i = reinterpret_cast<int*>(corr);                       // [M][units][2]
+        float* fac = corr + 2 * p.M * units_staged;                       // [M][units] 2^e
+        for (int base = 0; base < nch; base += CT * XB) {
+          uint4 v[XB];
+#pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            int t, il, jj, r;
+            v[b] = make_uint4(0u, 0u, 0u, 0u);
+            if (locate(base + b * CT + ctid, t, il, jj, r))
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+          }
+#pragma unroll
+          for (int b = 0; b < XB; ++b) {
+            const int q = base + b * CT + ctid;
+            int t, il, jj, r;
+            const bool ok = locate(q, t, il, jj, r);
+            const uint32_t rr[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+            float xf[8];
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+              xf[2 * e2] = __uint_as_float(rr[e2] << 16);
+              xf[2 * e2 + 1] = __uint_as_float(rr[e2] & 0xFFFF0000u);
+            }
+            float m = 0.f;
+#pragma unroll
+            for (int e2 = 0; e2 < 8; ++e2) m = fmaxf(m, fabsf(xf[e2]));
+#pragma unroll
+            for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
+            int e = 0;
+            if (m > 0.f) {
+              int ex;
+              frexpf(m, &ex);
+              e = min(max(ex - 14, -126), 114);
+            }
+            const float down = __int_as_float((127 - e) << 23);            // 2^-e, exact
+            int hd[8], ld[8], sh = 0, sl = 0;
+#pragma unroll
+            for (int e2 = 0; e2 < 8; ++e2) {
+              const int x16 = __float2int_rn(xf[e2] * down);
+              hd[e2] = (x16 + 128) >> 8;
+              ld[e2] = x16 - (hd[e2] << 8);
+              sh += hd[e2];
+              sl += ld[e2];
+            }
+            auto pack4 = [](int a, int b2, int c2, int d) {
+              return prmt(prmt(static_cast<uint32_t>(a), static_cast<uint32_t>(b2), 0x0040u),
+                          prmt(static_cast<uint32_t>(c2), static_cast<uint32_t>(d), 0x0040u), 0x5410u);
+            };
+            if (ok) {
+              const int uloc = il * RANGE_UNITS + (jj >> 4);
+              const int j = jj & 15, cq = j >> 2, i = j & 3;
+              const int T = t >> 2, tt = t & 3;
+              const int ncols = min(8, 2 * p.M - 8 * T);
+              uint8_t* base_p = xs + T * units_staged * 1024 + uloc * (ncols * 128) + (i >> 1) * (ncols * 64) +
+                                cq * 16 + (i & 1) * 8;
+              *reinterpret_cast<uint2*>(base_p + (2 * tt) * 64) =
+                  make_uint2(pack4(hd[0], hd[2], hd[4], hd[6]), pack4(hd[1], hd[3], hd[5], hd[7]));
+              *reinterpret_cast<uint2*>(base_p + (2 * tt + 1) * 64) =
+                  make_uint2(pack4(ld[0], ld[2], ld[4], ld[6]), pack4(ld[1], ld[3], ld[5], ld[7]));
+            }
+#pragma unroll
+            for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) {
+              sh += __shfl_xor_sync(0xffffffffu, sh, o2);
+              sl += __shfl_xor_sync(0xffffffffu, sl, o2);
+            }
+            if (ok && (jj % CPU) == 0) {
+              const int uloc = il * RANGE_UNITS + (jj >> 4);
+              corr_i[(t * units_staged + uloc) * 2] = 8 * sh;
+              corr_i[(t * units_staged + uloc) * 2 + 1] = 8 * sl;
+              fac[t * units_staged + uloc] = __int_as_float((127 + e) << 23);   // 2^e
+            }
           }
         }
         named_sync(1, CT);
@@ -486,7 +613,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       for (int h = 0; h < UPW; ++h) {
         sc[h][0] = sc[h][1] = 1.f;
         const int uu = u0 + gw + h * GW;
-        if (FMT == 2 && uu < uend) {
+        if (I4 && uu < uend) {
           sc[h][0] = __half2float(__ldg(p.s16 + rg * ng + uu));
           sc[h][1] = __half2float(__ldg(p.s16 + rg8 * ng + uu));
         }
@@ -510,9 +637,49 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[slot]);
-      float acc[MT][4];
+      float acc[MT][PW];
 #pragma unroll
-      for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int j = 0; j < PW; ++j) acc[t][j] = 0.f;
+      if constexpr (FMT == 20) {
+        const int* corr_i = reinterpret_cast<const int*>(corr);
+        const float* fac = corr + 2 * p.M * units_staged;
+        float accT[MT][2];
+#pragma unroll
+        for (int T = 0; T < MT; ++T) accT[T][0] = accT[T][1] = 0.f;
+#pragma unroll
+        for (int h = 0; h < UPW; ++h) {
+          const int uu = u0 + gw + h * GW;
+          if (uu >= uend) continue;
+          const int uloc = il * RANGE_UNITS + (uu - u0);
+          uint32_t Bq[MT][8];
+          int nc[MT][2];
+          float fT[MT];
+#pragma unroll
+          for (int T = 0; T < MT; ++T) {
+            const int ncols = min(8, 2 * p.M - 8 * T);
+            const uint32_t a = smem_u32(xs) + T * units_staged * 1024 + uloc * (ncols * 128) + g * 64 + c * 16;
+            const bool colok = g < ncols;
+            const uint4 b0 = lds_v4(colok ? a : zbase);
+            const uint4 b1 = lds_v4(colok ? a + ncols * 64 : zbase + 16);
+            Bq[T][0] = b0.x; Bq[T][1] = b0.y; Bq[T][2] = b0.z; Bq[T][3] = b0.w;
+            Bq[T][4] = b1.x; Bq[T][5] = b1.y; Bq[T][6] = b1.z; Bq[T][7] = b1.w;
+            const int tok = 4 * T + c;
+            if (tok < p.M) {
+              const int2 cv = *reinterpret_cast<const int2*>(corr_i + (tok * units_staged + uloc) * 2);
+              nc[T][0] = cv.x; nc[T][1] = cv.y;
+              fT[T] = fac[tok * units_staged + uloc];
+            } else {
+              nc[T][0] = nc[T][1] = 0;
+              fT[T] = 0.f;
+            }
+          }
+          unit_i8<MT>(wr[h][0], wr[h][1], Bq, nc, fT, sc[h][0], sc[h][1], accT);
+        }
+#pragma unroll
+        for (int T = 0; T < MT; ++T) { acc[T][0] = accT[T][0]; acc[T][1] = accT[T][1]; }
+      } else {
 #pragma unroll
       for (int h = 0; h < UPW; ++h) {
         const int uu = u0 + gw + h * GW;
@@ -533,29 +700,45 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
             Nl[t][j2] = tok < p.M ? -corr[tok * units_staged + uloc] : 0.f;
           }
         }
-        unit_mma<FMT, MT>(wr[h][0], wr[h][1], Bl, Nl, sc[h][0], sc[h][1], acc);
+        float a4[MT][4];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) { a4[t][0] = acc[t][0]; a4[t][1] = acc[t][1]; a4[t][2] = acc[t][2]; a4[t][3] = acc[t][3]; }
+        unit_mma<FMT, MT>(wr[h][0], wr[h][1], Bl, Nl, sc[h][0], sc[h][1], a4);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) { acc[t][0] = a4[t][0]; acc[t][1] = a4[t][1]; acc[t][2] = a4[t][2]; acc[t][3] = a4[t][3]; }
+      }
       }
 
       // -------------------------------------------------------------- the item's partial: four warps
       const int buf = n_it & 1;
       {
-        float* dst = gred + (((grp * 2 + buf) * GW + gw) * 32 + lane) * (4 * MT);
+        float* dst = gred + (((grp * 2 + buf) * GW + gw) * 32 + lane) * (PW * MT);
 #pragma unroll
-        for (int t = 0; t < MT; ++t)
-          *reinterpret_cast<float4*>(dst + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+        for (int t = 0; t < MT; ++t) {
+          if constexpr (PW == 4)
+            *reinterpret_cast<float4*>(dst + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+          else
+            *reinterpret_cast<float2*>(dst + 2 * t) = make_float2(acc[t][0], acc[t][1]);
+        }
       }
       named_sync(2 + grp, GW * 32);
       if (gw == (n_it % GW)) {
-        const float* src = gred + ((grp * 2 + buf) * GW) * 32 * (4 * MT);
+        const float* src = gred + ((grp * 2 + buf) * GW) * 32 * (PW * MT);
         for (int o = lane; o < 16 * p.M; o += 32) {
           const int orow = o & 15, otok = o >> 4;
-          const int tt = otok >> 3, tk = otok & 7;
-          const int src_lane = (orow & 7) * 4 + (tk >> 1);
-          const int reg = tt * 4 + (orow >> 3) * 2 + (tk & 1);
+          int src_lane, reg;
+          if constexpr (FMT == 20) {          // 4-token tiles: token 4T + c in lane (row & 7) * 4 + c
+            src_lane = (orow & 7) * 4 + (otok & 3);
+            reg = (otok >> 2) * 2 + (orow >> 3);
+          } else {                           // 8-token tiles: tokens 2c, 2c + 1 in lane (row & 7) * 4 + c
+            const int tt = otok >> 3, tk = otok & 7;
+            src_lane = (orow & 7) * 4 + (tk >> 1);
+            reg = tt * 4 + (orow >> 3) * 2 + (tk & 1);
+          }
           float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < GW; ++w) v += src[(w * 32 + src_lane) * (4 * MT) + reg];
-          v *= xsc[otok * MAX_RANGES + r];
+          for (int w = 0; w < GW; ++w) v += src[(w * 32 + src_lane) * (PW * MT) + reg];
+          if constexpr (FMT != 20) v *= xsc[otok * MAX_RANGES + r];
           if (direct) {
             const int64_t n = row0 + orow;
             if (n < p.N) store_out<FMT>(p, n, otok, v);
@@ -689,9 +872,13 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.R = 1; p.C = 1; p.slots = 2; p.max_items = 0;
   p.dst = dst ? *dst : OutRanks{};
   // one token tile: three groups (12 warps + producer) and six ring slots; two token tiles: two groups
-  if (fmt == 2)
+  // int4: one token on the integer tensor path (half the MMAs, a third of the dequantisation work); more
+  // tokens on the bf16 path, whose n8 tile holds eight tokens
+  if (fmt == 2) {
+    if (M == 1) return launch_gemv_t<20, 1, 3, 1>(p, sms, 1, 6, pdl, st);
     return M <= 8 ? launch_gemv_t<2, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                   : launch_gemv_t<2, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
+  }
   if (fmt == 5)
     return M <= 8 ? launch_gemv_t<5, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                   : launch_gemv_t<5, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
