@@ -57,6 +57,9 @@ SIGNATURES = [
                                ctypes.c_uint, _P]),
     ("lb_rank_barrier", _I, [ctypes.POINTER(_P), _I, _I, ctypes.c_uint32, ctypes.c_uint32, _P]),
     ("lb_rmsnorm", _I, [_P, _I64, _I64, _P, _I, ctypes.c_float, ctypes.c_float, _P, _P]),
+    ("lb_linear_rms_workspace_size", _I, [_I, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
+    ("lb_linear_rms", _I, [_I, _P, _I64, _I64, _P, _I, ctypes.c_float, ctypes.c_float, _P, _P, _I64, _P, _I, _P, _I64,
+                           _P, _SZ, ctypes.c_uint, _P]),
     ("lb_qkv_prep", _I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, ctypes.c_float, _P, _I64, _P, _I64, _I64, _I64,
                          _P, _P, _I64, _I64, _P]),
     ("lb_act_mul", _I, [_P, _I64, _I64, _I, _P, _P]),

@@ -41,6 +41,7 @@ __device__ __forceinline__ uint16_t tobf(float f) {
 
 // One CTA per (token, head of q / k / v); blockDim = 128 >= dh / 2 (one thread per rotated pair).
 __global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepParams p) {
+  pdl_launch_dependents();
   const int per = p.nh + 2 * p.kvh;
   const int64_t bt = blockIdx.x / per;
   const int hh = blockIdx.x % per;
@@ -91,6 +92,7 @@ __device__ __forceinline__ float act(float g) {
 template <int KIND>
 __global__ void __launch_bounds__(256) act_mul_kernel(const uint16_t* __restrict__ gu, int64_t M, int64_t I,
                                                       uint16_t* __restrict__ out, int vec) {
+  pdl_launch_dependents();   // the down projection's GEMV may start streaming its weights (it waits for this grid)
   if (vec) {
     const int64_t n8 = M * (I / 8);
     for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n8;

@@ -305,7 +305,7 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
 // Argument checks and dispatch shared by lb_linear_ex and lb_linear_sharded (dst: column-sharded outputs).
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,
                        const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
-                       unsigned flags, void* stream, const OutRanks* dst) {
+                       unsigned flags, void* stream, const OutRanks* dst, const RmsPrologue* ln = nullptr) {
   if (!has_product(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (flags & ~static_cast<unsigned>(LB_LINEAR_STATIC_WEIGHTS)) return fail(LB_E_ARG, "lb_linear: unknown flags");
@@ -333,7 +333,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool pdl = (flags & LB_LINEAR_STATIC_WEIGHTS) != 0;
   if (use_gemv(M))
-    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, pdl, st, dst), "gemv");
+    return launched(launch_gemv(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, d->sms, pdl, st, dst, ln),
+                    "gemv");
   const char* why = nullptr;
   cudaError_t e = launch_gemm(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, d->sms, st, &why, dst);
   if (e != cudaSuccess && why) return fail(LB_E_LAUNCH, "gemm: %s (%s)", why, cudaGetErrorString(e));
@@ -351,6 +352,42 @@ int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, c
               const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
               void* stream) {
   return lb_linear_ex(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, ws_bytes, 0u, stream);
+}
+
+static size_t rms_rows_bytes(int64_t M, int64_t K) { return (static_cast<size_t>(M) * K * 2 + 255) & ~static_cast<size_t>(255); }
+
+int lb_linear_rms_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes) {
+  int r = lb_linear_workspace_size(fmt, M, N, K, bytes);
+  if (r) return r;
+  if (!use_gemv(M)) *bytes += rms_rows_bytes(M, K);
+  return LB_OK;
+}
+
+int lb_linear_rms(int fmt, const void* x, int64_t M, int64_t K, const void* ln_w, int ln_dtype, float eps, float off,
+                  const void* codes, const void* scales, int64_t N, const void* bias, int accumulate, void* y,
+                  int64_t ldy, void* workspace, size_t ws_bytes, unsigned flags, void* stream) {
+  if (!ln_w) return fail(LB_E_ARG, "lb_linear_rms: ln_w is required");
+  if (ln_dtype != LB_DT_F32 && ln_dtype != LB_DT_BF16) return fail(LB_E_ARG, "lb_linear_rms: ln_dtype must be F32 or BF16");
+  if (!aligned(ln_w, ln_dtype == LB_DT_F32 ? 4 : 2)) return fail(LB_E_ALIGN, "lb_linear_rms: ln_w must be element aligned");
+  if (use_gemv(M)) {
+    const RmsPrologue ln{ln_w, ln_dtype == LB_DT_F32 ? 1 : 0, eps, off};
+    return linear_impl(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, nullptr, 0, flags, stream, nullptr,
+                       &ln);
+  }
+  // prefill: the normalised rows go to the front of the workspace, the product's own workspace follows
+  if (!x || !codes || !scales || !y) return fail(LB_E_ARG, "lb_linear: x, codes, scales and y are required");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear: M, N, K must be positive");
+  size_t need = 0;
+  int r = lb_linear_rms_workspace_size(fmt, M, N, K, &need);
+  if (r) return r;
+  if (!workspace || ws_bytes < need)
+    return fail(LB_E_WORKSPACE, "lb_linear_rms: workspace of %zu bytes needed (got %zu)", need, workspace ? ws_bytes : 0);
+  if (!aligned(workspace, 256)) return fail(LB_E_ALIGN, "lb_linear_rms: workspace must be 256-byte aligned");
+  r = lb_rmsnorm(x, M, K, ln_w, ln_dtype, eps, off, workspace, stream);
+  if (r) return r;
+  const size_t head = rms_rows_bytes(M, K);
+  return linear_impl(fmt, workspace, M, K, codes, scales, N, bias, accumulate, y, ldy,
+                     static_cast<char*>(workspace) + head, ws_bytes - head, flags, stream, nullptr);
 }
 
 int lb_interleave_cols(const void* src, int G, int64_t M, int64_t Nl, void* dst, void* stream) {

@@ -273,4 +273,126 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   return v;
 }
 
+// ---- RMSNorm in one fixed order, shared by the standalone norm and the norm prologue of the decode GEMV, so
+// that a fused and an unfused normalised projection give the same bits.  A row of K bf16 values is cut into
+// 16-byte chunks of 8 values; virtual thread v of 256 (eight warps of 32) adds the squares of chunks v, v + 256,
+// v + 512, ... with fmaf in value order; each virtual warp adds its 32 lanes by the xor butterfly 16, 8, 4, 2, 1;
+// the eight warp sums are added in warp order; fac = 1 / sqrt(sum / K + eps).
+constexpr int RMS_VT = 256;   // virtual threads of the reduction
+
+__device__ __forceinline__ float rms_chunk_fma(const uint4& v, float s) {
+  const uint32_t r[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float a = __uint_as_float(r[e] << 16), b = __uint_as_float(r[e] & 0xFFFF0000u);
+    s = fmaf(a, a, s);
+    s = fmaf(b, b, s);
+  }
+  return s;
+}
+
+// chunk j of a row (values 8j .. 8j + 7, zeros past K); `vec`: the row is 16-byte aligned and K % 8 == 0
+__device__ __forceinline__ uint4 rms_load_chunk(const uint16_t* row, int64_t K, int64_t j, bool vec) {
+  if (vec) return ldg_nc_v4(row + 8 * j);
+  uint32_t r[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int64_t k = 8 * j + 2 * e;
+    const uint32_t a = k < K ? row[k] : 0u, b = k + 1 < K ? row[k + 1] : 0u;
+    r[e] = a | (b << 16);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+__device__ __forceinline__ float rms_butterfly(float s) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+__device__ __forceinline__ float rms_factor(float tot, int64_t K, float eps) {
+  return 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+}
+
+// The whole reduction of one row by one warp (lane l plays virtual threads l, l + 32, ..., l + 224): each pass
+// loads the next chunk of all eight virtual threads at once, so the loads of a pass are in flight together.
+__device__ __forceinline__ float rms_row_factor_warp(const uint16_t* row, int64_t K, float eps, bool vec) {
+  constexpr int NW = RMS_VT / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t nc = (K + 7) / 8;
+  float s[NW];
+#pragma unroll
+  for (int w = 0; w < NW; ++w) s[w] = 0.f;
+  for (int64_t j0 = lane; j0 < nc; j0 += RMS_VT) {
+    uint4 v[NW];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const int64_t j = j0 + 32 * w;
+      v[w] = j < nc ? rms_load_chunk(row, K, j, vec) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      if (j0 + 32 * w < nc) s[w] = rms_chunk_fma(v[w], s[w]);
+  }
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) tot += rms_butterfly(s[w]);
+  return rms_factor(tot, K, eps);
+}
+
+// The 8 RMSNorm weights at element k0 (float32: a, b; bf16: a), 16-byte aligned loads when `vec`.
+struct RmsW {
+  uint4 a, b;
+};
+__device__ __forceinline__ RmsW rms_load_w(const void* w, bool w_f32, int64_t k0, int64_t K, bool vec) {
+  RmsW r;
+  if (vec && w_f32) {
+    r.a = ldg_nc_v4(static_cast<const float*>(w) + k0);
+    r.b = ldg_nc_v4(static_cast<const float*>(w) + k0 + 4);
+  } else if (vec) {
+    r.a = ldg_nc_v4(static_cast<const uint16_t*>(w) + k0);
+    r.b = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    uint32_t f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int64_t k = k0 + e < K ? k0 + e : K - 1;
+      f[e] = w_f32 ? __float_as_uint(static_cast<const float*>(w)[k])
+                   : static_cast<uint32_t>(static_cast<const uint16_t*>(w)[k]);
+    }
+    if (w_f32) {
+      r.a = make_uint4(f[0], f[1], f[2], f[3]);
+      r.b = make_uint4(f[4], f[5], f[6], f[7]);
+    } else {
+      r.a = make_uint4(f[0] | (f[1] << 16), f[2] | (f[3] << 16), f[4] | (f[5] << 16), f[6] | (f[7] << 16));
+      r.b = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  return r;
+}
+
+// The normalised chunk: each value bf16((x * fac) * (w + off)).
+__device__ __forceinline__ uint4 rms_apply_chunk(const uint4& v, float fac, const RmsW& w, bool w_f32, float off) {
+  float wf[8];
+  if (w_f32) {
+    wf[0] = __uint_as_float(w.a.x); wf[1] = __uint_as_float(w.a.y); wf[2] = __uint_as_float(w.a.z);
+    wf[3] = __uint_as_float(w.a.w); wf[4] = __uint_as_float(w.b.x); wf[5] = __uint_as_float(w.b.y);
+    wf[6] = __uint_as_float(w.b.z); wf[7] = __uint_as_float(w.b.w);
+  } else {
+    const uint32_t r[4] = {w.a.x, w.a.y, w.a.z, w.a.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { wf[2 * e] = __uint_as_float(r[e] << 16); wf[2 * e + 1] = __uint_as_float(r[e] & 0xFFFF0000u); }
+  }
+  const uint32_t r[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float ya = __uint_as_float(r[e] << 16) * fac * (wf[2 * e] + off);
+    const float yb = __uint_as_float(r[e] & 0xFFFF0000u) * fac * (wf[2 * e + 1] + off);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(ya, yb);
+    o[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 }  // namespace lb

@@ -69,6 +69,9 @@ struct GemvParams {
   int slots;              // ring slots
   int max_items;          // item partials per CTA (shared-memory table), 0 = outputs written directly
   OutRanks dst;           // column-sharded layer: every rank's output (dst.n == 0: y)
+  const void* ln;         // RMSNorm weights [K] (float32 or bf16) of the norm prologue, or null
+  int ln_f32, ln_vec;     // weights are float32; weights are 16-byte aligned
+  float ln_eps, ln_off;
 };
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
@@ -234,7 +237,7 @@ __device__ __forceinline__ void unit_i8(const uint4& w0, const uint4& w8, const 
 
 // Shared-memory carve-up, in bytes from the base of dynamic shared memory.
 struct GemvSmem {
-  int ring, xs, corr, xsc, gred, ptab, zeros, bars, total;
+  int ring, xs, corr, xsc, gred, ptab, zeros, bars, lnf, total;
   int token_stride;   // bytes of one token's staged activations
 };
 
@@ -252,7 +255,8 @@ __host__ __device__ inline GemvSmem gemv_smem(int fmt, int M, int MT, int G, int
   s.ptab = s.gred + G * 2 * GW * 32 * (fmt == 20 ? 2 : 4) * MT * 4;   // double-buffered group partials
   s.zeros = s.ptab + ((items * 16 * M * 4 + 127) & ~127);
   s.bars = s.zeros + 256;                                      // 256 zero bytes (absent tokens)
-  s.total = s.bars + 2 * MAX_SLOTS * 8 + 16;
+  s.lnf = s.bars + 2 * MAX_SLOTS * 8 + 16;                    // [16] RMSNorm factors per token
+  s.total = s.lnf + 64;
   return s;
 }
 
@@ -364,6 +368,15 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     // ------------------------------------------------------------------ consumers
     pdl_wait();                             // the activations (and the output) come from earlier kernels
     const int ctid = threadIdx.x;
+    float* lnf = reinterpret_cast<float*>(dyn_smem + L.lnf);
+    if (p.ln) {
+      // norm prologue: one warp per token reduces the whole row (every K range) in the order of lb_rmsnorm
+      for (int t = warp; t < p.M; t += NCW) {
+        const float f = rms_row_factor_warp(p.x + static_cast<int64_t>(t) * p.K, p.K, p.ln_eps, true);
+        if (lane == 0) lnf[t] = f;
+      }
+      named_sync(1, CT);
+    }
     // Stage the activations of this CTA's ranges: per (token, range) power-of-two factor, fp16, B-fragment
     // order, and the offset correction per (token, unit).  Pass 1 loads XB chunks per thread at a time, parks
     // each raw chunk in its final slot and takes the absmax per (token, range); pass 2 converts the chunks in
@@ -393,12 +406,23 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
         // B-fragment order; one pass, the offset correction 136 * sum(x) per (token, unit)
         for (int base = 0; base < nch; base += CT * XB) {
           uint4 v[XB];
+          RmsW wv[XB];
 #pragma unroll
           for (int b = 0; b < XB; ++b) {
             int t, il, jj, r;
             v[b] = make_uint4(0u, 0u, 0u, 0u);
-            if (locate(base + b * CT + ctid, t, il, jj, r))
-              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+            if (locate(base + b * CT + ctid, t, il, jj, r)) {
+              const int64_t k0 = static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8;
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + k0);
+              if (p.ln) wv[b] = rms_load_w(p.ln, p.ln_f32 != 0, k0, p.K, p.ln_vec != 0);
+            }
+          }
+          if (p.ln) {                            // norm prologue: bf16((x * fac) * (w + off)), as lb_rmsnorm
+#pragma unroll
+            for (int b = 0; b < XB; ++b) {
+              int t, il, jj, r;
+              if (locate(base + b * CT + ctid, t, il, jj, r)) v[b] = rms_apply_chunk(v[b], lnf[t], wv[b], p.ln_f32 != 0, p.ln_off);
+            }
           }
 #pragma unroll
           for (int b = 0; b < XB; ++b) {
@@ -430,12 +454,23 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
         float* fac = corr + 2 * p.M * units_staged;                       // [M][units] 2^e
         for (int base = 0; base < nch; base += CT * XB) {
           uint4 v[XB];
+          RmsW wv[XB];
 #pragma unroll
           for (int b = 0; b < XB; ++b) {
             int t, il, jj, r;
             v[b] = make_uint4(0u, 0u, 0u, 0u);
-            if (locate(base + b * CT + ctid, t, il, jj, r))
-              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+            if (locate(base + b * CT + ctid, t, il, jj, r)) {
+              const int64_t k0 = static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8;
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + k0);
+              if (p.ln) wv[b] = rms_load_w(p.ln, p.ln_f32 != 0, k0, p.K, p.ln_vec != 0);
+            }
+          }
+          if (p.ln) {                            // norm prologue: bf16((x * fac) * (w + off)), as lb_rmsnorm
+#pragma unroll
+            for (int b = 0; b < XB; ++b) {
+              int t, il, jj, r;
+              if (locate(base + b * CT + ctid, t, il, jj, r)) v[b] = rms_apply_chunk(v[b], lnf[t], wv[b], p.ln_f32 != 0, p.ln_off);
+            }
           }
 #pragma unroll
           for (int b = 0; b < XB; ++b) {
@@ -503,12 +538,23 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       } else {
       for (int base = 0; base < nch; base += CT * XB) {        // pass 1
           uint4 v[XB];
+          RmsW wv[XB];
   #pragma unroll
           for (int b = 0; b < XB; ++b) {
             int t, il, jj, r;
             v[b] = make_uint4(0u, 0u, 0u, 0u);
-            if (locate(base + b * CT + ctid, t, il, jj, r))
-              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8);
+            if (locate(base + b * CT + ctid, t, il, jj, r)) {
+              const int64_t k0 = static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8;
+              v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + k0);
+              if (p.ln) wv[b] = rms_load_w(p.ln, p.ln_f32 != 0, k0, p.K, p.ln_vec != 0);
+            }
+          }
+          if (p.ln) {                            // norm prologue: bf16((x * fac) * (w + off)), as lb_rmsnorm
+#pragma unroll
+            for (int b = 0; b < XB; ++b) {
+              int t, il, jj, r;
+              if (locate(base + b * CT + ctid, t, il, jj, r)) v[b] = rms_apply_chunk(v[b], lnf[t], wv[b], p.ln_f32 != 0, p.ln_off);
+            }
           }
   #pragma unroll
           for (int b = 0; b < XB; ++b) {
@@ -855,7 +901,7 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
 
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st, const OutRanks* dst) {
+                        cudaStream_t st, const OutRanks* dst, const RmsPrologue* ln) {
   GemvParams p;
   p.x = reinterpret_cast<const uint16_t*>(x);
   p.w = reinterpret_cast<const uint8_t*>(codes);
@@ -871,6 +917,11 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.nr = (p.total_units + gemv::RANGE_UNITS - 1) / gemv::RANGE_UNITS;
   p.R = 1; p.C = 1; p.slots = 2; p.max_items = 0;
   p.dst = dst ? *dst : OutRanks{};
+  p.ln = ln ? ln->w : nullptr;
+  p.ln_f32 = ln ? ln->w_f32 : 0;
+  p.ln_vec = (ln && (reinterpret_cast<uintptr_t>(ln->w) & 15) == 0) ? 1 : 0;
+  p.ln_eps = ln ? ln->eps : 0.f;
+  p.ln_off = ln ? ln->off : 0.f;
   // one token tile: three groups (12 warps + producer) and six ring slots; two token tiles: two groups
   // int4: one token on the integer tensor path (half the MMAs, a third of the dequantisation work); more
   // tokens on the bf16 path, whose n8 tile holds eight tokens

@@ -28,9 +28,16 @@ cudaError_t launch_dequant(int fmt, const void* codes, const void* scales, int s
                            void* out, int out_dt, int sms, cudaStream_t st);
 
 int gemv_max_k(int fmt);
+// RMSNorm prologue of a normalised projection (the rows of x are normalised before the product)
+struct RmsPrologue {
+  const void* w;   // [K] float32 or bf16
+  int w_f32;
+  float eps, off;
+};
+
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st, const OutRanks* dst = nullptr);
+                        cudaStream_t st, const OutRanks* dst = nullptr, const RmsPrologue* ln = nullptr);
 
 size_t gemm_workspace_bytes(int64_t M, int64_t K);
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,

@@ -3,7 +3,9 @@
 // as hub_gpu's rms op and the norm prologue of its gemvq*n kernels compute it (apsi/hub_gpu.py:1690-1693,
 // 837-870; launched by _Base.linear with ln=..., apsi/hub_gpu.py:1305-1315).  The normalised rows are rounded
 // to bfloat16 once, because the product kernels take bf16 activations.  One CTA per row; the sum of squares
-// uses a fixed reduction tree (the same bits on every launch).  HBM-bound: 2 bytes read + 2 written per value.
+// uses the fixed reduction order of rms_chunk_fma / rms_butterfly (lb_common.cuh), the same one the decode
+// GEMV's norm prologue uses, so lb_linear_rms gives the bits of lb_rmsnorm + lb_linear.  HBM-bound: 2 bytes
+// read + 2 written per value.
 #include "../../include/apsi_lowbit.h"
 #include "lb_common.cuh"
 #include "lb_kernels.h"
@@ -11,33 +13,37 @@
 namespace lb {
 
 template <int WDT>   // LB_DT_F32 or LB_DT_BF16 weights
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, int64_t K,
-                                                      const void* __restrict__ wv, float eps, float off,
-                                                      uint16_t* __restrict__ out) {
-  __shared__ float red[8];
+__global__ void __launch_bounds__(RMS_VT) rmsnorm_kernel(const uint16_t* __restrict__ x, int64_t K,
+                                                         const void* __restrict__ wv, float eps, float off,
+                                                         uint16_t* __restrict__ out, int vec, int wvec) {
+  __shared__ float red[RMS_VT / 32];
+  pdl_launch_dependents();   // a following static-weight GEMV may start streaming its weights now (it waits for
+                             // this grid before it reads the normalised rows)
   const int64_t row = blockIdx.x;
   const uint16_t* xr = x + row * K;
   uint16_t* orow = out + row * K;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  auto bf = [](uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); };
+  const int64_t nc = (K + 7) / 8;
   float ss = 0.f;
-  for (int64_t k = tid; k < K; k += 256) {
-    const float v = bf(xr[k]);
-    ss = fmaf(v, v, ss);
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  for (int64_t j = tid; j < nc; j += RMS_VT) ss = rms_chunk_fma(rms_load_chunk(xr, K, j, vec), ss);
+  ss = rms_butterfly(ss);
   if (lane == 0) red[warp] = ss;
   __syncthreads();
   float tot = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  const float fac = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-  for (int64_t k = tid; k < K; k += 256) {
-    const float w = (WDT == LB_DT_F32) ? static_cast<const float*>(wv)[k] : bf(static_cast<const uint16_t*>(wv)[k]);
-    const float y = bf(xr[k]) * fac * (w + off);
-    __nv_bfloat16 h = __float2bfloat16_rn(y);
-    orow[k] = *reinterpret_cast<uint16_t*>(&h);
+  for (int i = 0; i < RMS_VT / 32; ++i) tot += red[i];
+  const float fac = rms_factor(tot, K, eps);
+  for (int64_t j = tid; j < nc; j += RMS_VT) {
+    const RmsW w = rms_load_w(wv, WDT == LB_DT_F32, 8 * j, K, wvec);
+    const uint4 y = rms_apply_chunk(rms_load_chunk(xr, K, j, vec), fac, w, WDT == LB_DT_F32, off);
+    if (vec) {
+      *reinterpret_cast<uint4*>(orow + 8 * j) = y;
+    } else {
+      const uint32_t r[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (8 * j + e < K) orow[8 * j + e] = static_cast<uint16_t>(r[e >> 1] >> (16 * (e & 1)));
+    }
   }
 }
 
@@ -58,9 +64,11 @@ extern "C" int lb_rmsnorm(const void* x, int64_t M, int64_t K, const void* w, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   uint16_t* ob = static_cast<uint16_t*>(out);
+  const int vec = (K % 8 == 0 && aligned(x, 16) && aligned(out, 16)) ? 1 : 0;
+  const int wvec = (vec && aligned(w, 16)) ? 1 : 0;
   if (w_dtype == LB_DT_F32)
-    rmsnorm_kernel<LB_DT_F32><<<static_cast<unsigned>(M), 256, 0, st>>>(xb, K, w, eps, off, ob);
+    rmsnorm_kernel<LB_DT_F32><<<static_cast<unsigned>(M), RMS_VT, 0, st>>>(xb, K, w, eps, off, ob, vec, wvec);
   else
-    rmsnorm_kernel<LB_DT_BF16><<<static_cast<unsigned>(M), 256, 0, st>>>(xb, K, w, eps, off, ob);
+    rmsnorm_kernel<LB_DT_BF16><<<static_cast<unsigned>(M), RMS_VT, 0, st>>>(xb, K, w, eps, off, ob, vec, wvec);
   return launched(cudaGetLastError(), "rmsnorm");
 }

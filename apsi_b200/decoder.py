@@ -13,9 +13,11 @@ apsi/hub_models.py:1018-1092), one block per layer:
 
 All projections -- QKV, O, gate/up, down and the LM head -- are int4 group-128 (or int8 per-row) weights in
 the library's packed layout, multiplied by ``kernels.linear``: the decode GEMV for up to 16 rows, the tcgen05
-GEMM above; the residual adds are the kernels' accumulate epilogue.  The norms (``lb_rmsnorm``), the QKV split
-with rotary embedding and the cache write (``lb_qkv_prep``) and the SwiGLU product (``lb_act_mul``) are the
-library's kernels too.  Embedding lookup and attention over the KV cache are torch operations (attention is not
+GEMM above; the residual adds are the kernels' accumulate epilogue.  The normalised projections (QKV,
+gate/up, head) go through ``kernels.linear_rms``: for decode the RMSNorm runs inside the GEMV's activation
+staging, for prefill ``lb_rmsnorm`` precedes the GEMM (the same bits either way).  The QKV split with rotary
+embedding and the cache write (``lb_qkv_prep``) and the SwiGLU product (``lb_act_mul``) are the library's
+kernels too.  Embedding lookup and attention over the KV cache are torch operations (attention is not
 on the quantized-linear path this library rebuilds).  Activations are bf16; the KV cache is bf16.
 
 Weights are random (seeded, N(0, 0.02) projections, unit norms), as configs[3] specifies; there is no
@@ -72,7 +74,10 @@ class _Proj:
         else:
             self.codes, self.scales, _ = Kn.quant_int8_rows(W, want_scale32=False)
 
-    def __call__(self, x, out=None, accumulate=False, static=False):
+    def __call__(self, x, out=None, accumulate=False, static=False, ln=None, eps=1e-6):
+        if ln is not None:                       # RMSNorm prologue (inside the decode GEMV for M <= 16)
+            return Kn.linear_rms(self.fmt, x, ln, self.codes, self.scales, self.N, eps=eps, out=out,
+                                 accumulate=accumulate, static_weights=static)
         return Kn.linear(self.fmt, x, self.codes, self.scales, self.N, out=out, accumulate=accumulate,
                          static_weights=static)
 
@@ -135,8 +140,7 @@ class QuantDecoder:
         cfg, Ld = self.cfg, self.layers[i]
         M = B * T
         static = M <= 16
-        xn = Kn.rmsnorm(X, Ld["ln1"], eps=cfg.eps)
-        qkv = Ld["qkv"](xn, static=static)
+        qkv = Ld["qkv"](X, static=static, ln=Ld["ln1"], eps=cfg.eps)
         kc, vc = cache.k[i], cache.v[i]                                # [B, kvh, cap, dh]
         q = torch.empty((B, cfg.nh, T, cfg.dh), dtype=torch.bfloat16, device=self.dev)
         Kn.qkv_prep(qkv, B, T, cfg.nh, cfg.kvh, cfg.dh, cfg.dh, self._cos, self._sin, q, kc, vc,
@@ -148,14 +152,12 @@ class QuantDecoder:
             attn = F.scaled_dot_product_attention(q, kc, vc, attn_mask=mask, enable_gqa=True)
         o_in = attn.transpose(1, 2).reshape(M, cfg.nh * cfg.dh).contiguous()
         Ld["o"](o_in, out=X, accumulate=True, static=static)
-        xn2 = Kn.rmsnorm(X, Ld["ln2"], eps=cfg.eps)
-        gu = Ld["gu"](xn2, static=static)
+        gu = Ld["gu"](X, static=static, ln=Ld["ln2"], eps=cfg.eps)
         m = Kn.act_mul(gu, cfg.I, 0)
         Ld["down"](m, out=X, accumulate=True, static=static)
 
     def _logits(self, X_last):
-        xn = Kn.rmsnorm(X_last.contiguous(), self.norm, eps=self.cfg.eps)
-        return self.head(xn, static=X_last.shape[0] <= 16)
+        return self.head(X_last.contiguous(), static=X_last.shape[0] <= 16, ln=self.norm, eps=self.cfg.eps)
 
     # ------------------------------------------------------------------ forward passes
     def prefill(self, ids, cache):
@@ -171,7 +173,9 @@ class QuantDecoder:
         """tok [B] int64, pos_t [1] int64 (device) -> logits [B, V]; writes cache slot pos_t."""
         B = tok.shape[0]
         X = self.embed.index_select(0, tok).contiguous()
-        mask = (torch.arange(cache.cap, device=self.dev) <= pos_t)[None, None, None, :]
+        # additive mask, built once per step (a boolean mask would be converted in every layer's attention)
+        mask = torch.zeros((1, 1, 1, cache.cap), dtype=torch.bfloat16, device=self.dev)
+        mask.masked_fill_(torch.arange(cache.cap, device=self.dev) > pos_t, float("-inf"))
         for i in range(self.cfg.L):
             self._block(i, X, B, 1, cache, pos_t, None, mask)
         return self._logits(X)

@@ -11,8 +11,9 @@ its kernels:
   ``precision.quantize``.  The reference's g32 ggml formats and minifloats are not products here and raise.
 * ``linear(m, X, Y, T, bias=None, acc=False, ln=None, eps=1e-6, off=0.0, xoff=0)`` -- ``Y (+)= norm(X) @ W.T
   (+ bias)`` for T rows: the decode GEMV for T <= 16, the tcgen05 GEMM above.  With ``ln`` (RMSNorm weights)
-  the rows are first normalised by ``lb_rmsnorm`` into a workspace (``x / sqrt(mean(x^2) + eps) * (ln + off)``,
-  float32 arithmetic, rounded once to bf16), as the reference's GEMM path does with its ``rms`` op.
+  the rows are first normalised (``x / sqrt(mean(x^2) + eps) * (ln + off)``, float32 arithmetic, rounded once
+  to bf16) by ``lb_linear_rms``: inside the decode GEMV's activation staging for T <= 16 (the reference's
+  gemvq*n kernels), by ``lb_rmsnorm`` into a workspace before the GEMM above (its ``rms`` op).
 * ``rms(X, Y, W, rows, n, eps, off, xoff=0, yoff=0)`` -- that normalisation on its own.
 * ``gemv``, ``gemm``, ``matmul``, ``matmul_rows`` -- the same product under the reference's other names.
 
@@ -156,15 +157,17 @@ class Ops:
     def linear(self, m, X, Y, T, bias=None, acc=False, ln=None, eps=1e-6, off=0.0, xoff=0):
         """Y (+)= norm(X) @ W.T (+ bias) for T rows (X: [T, cols] from element xoff, Y: [T, rows]); ln: RMSNorm
         weights applied to each row of X first."""
-        if ln is not None:
-            Z = self.ws("lnx", T * m.cols)
-            self.rms(X, Z, ln, T, m.cols, eps, off, xoff=xoff)
-            X, xoff = Z, 0
         if X.n < xoff + T * m.cols or Y.n < T * m.rows:
             raise LowbitError(LB_E_ARG, "linear: buffers too small for T rows")
         x = X.t[xoff:xoff + T * m.cols].view(T, m.cols)
         y = Y.t[:T * m.rows].view(T, m.rows)
         b = bias.t[:m.rows] if bias is not None else None
+        if ln is not None:                       # the norm inside the decode GEMV (T <= 16), else lb_rmsnorm first
+            if ln.n < m.cols:
+                raise LowbitError(LB_E_ARG, "linear: ln holds fewer than cols values")
+            _k.linear_rms(m.fmt, x, ln.t[:m.cols], m.buf, m.scales, m.rows, eps=eps, off=off, bias=b, out=y,
+                          accumulate=bool(acc))
+            return
         _k.linear(m.fmt, x, m.buf, m.scales, m.rows, bias=b, out=y, accumulate=bool(acc))
 
     def gemv(self, m, X, Y, T, xoff=0, yoff=0, bias=None, acc=False, ln=None, eps=1e-6, off=0.0):

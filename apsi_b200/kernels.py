@@ -391,6 +391,43 @@ def rmsnorm(x, w, eps=1e-6, off=0.0, out=None):
     return out
 
 
+def linear_rms(fmt, x, ln, codes, scales, N, eps=1e-6, off=0.0, bias=None, out=None, accumulate=False,
+               static_weights=False):
+    """y[M, N] = rmsnorm(x; ln, eps, off) . deq(W)^T (+ bias) (+ out if accumulate): the bits of ``rmsnorm``
+    followed by ``linear``.  For M <= 16 the norm runs inside the decode GEMV (one launch); above, the normalised
+    rows go through a workspace.  ``ln``: float32 or bfloat16 [K] CUDA tensor."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise LowbitError(_lib.LB_E_ARG, "x must be a contiguous bfloat16 tensor")
+    K = x.shape[-1]
+    M = x.numel() // K
+    dev = x.device
+    if not (isinstance(ln, torch.Tensor) and ln.device == dev and ln.dtype in (torch.float32, torch.bfloat16)
+            and ln.is_contiguous()):
+        ln = ln.to(dev)
+        ln = (ln if ln.dtype in (torch.float32, torch.bfloat16) else ln.float()).contiguous()
+    if ln.numel() < K:
+        raise LowbitError(_lib.LB_E_ARG, f"ln holds {ln.numel()} values, K is {K}")
+    if out is None:
+        if accumulate:
+            raise LowbitError(_lib.LB_E_ARG, "accumulate needs an output tensor")
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ldy = out.stride(-2) if out.dim() >= 2 else N
+    wdt = _lib.DT_F32 if ln.dtype == torch.float32 else _lib.DT_BF16
+    with torch.cuda.device(dev):
+        nbytes = 0
+        if M > 16:
+            n = ctypes.c_size_t(0)
+            _lib.call("lb_linear_rms_workspace_size", fmt, M, N, K, ctypes.byref(n))
+            nbytes = n.value
+        ws = _workspace(dev, nbytes) if nbytes else None
+        _lib.call("lb_linear_rms", fmt, _ptr(x), M, K, _ptr(ln), wdt, ctypes.c_float(eps), ctypes.c_float(off),
+                  _ptr(codes), _ptr(scales), N, _ptr(bias) if bias is not None else None, 1 if accumulate else 0,
+                  _ptr(out), ldy, _ptr(ws) if ws is not None else None, nbytes,
+                  _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0, _stream(dev))
+    return out
+
+
 def qkv_prep(qkv, B, T, nh, kvh, dh, rot, cos, sin, q_out, k_cache, v_cache, pos0=None, start=0, qn=None, kn=None,
              eps=1e-6):
     """Split / (optionally) RMSNorm / rotate the fused QKV projection; q_out [B, nh, T, dh]; k_cache, v_cache

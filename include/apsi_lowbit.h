@@ -167,6 +167,18 @@ int lb_gguf_decode(int kind, const uint8_t* blocks, int64_t n, float* out, void*
 int lb_rmsnorm(const void* x, int64_t M, int64_t K, const void* w, int w_dtype, float eps, float off, void* out,
                void* stream);
 
+/* Bytes of device workspace lb_linear_rms needs for this shape (0 for M <= 16). */
+int lb_linear_rms_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes);
+
+/* A normalised projection: y (+)= rmsnorm(x; ln_w, eps, off) . deq(W)^T (+ bias), the result of lb_rmsnorm
+ * followed by lb_linear_ex, bit for bit.  M <= 16: the norm runs inside the decode GEMV's activation staging
+ * (one launch, no workspace, x itself is not modified); M > 16: lb_rmsnorm into the front of `workspace`, then
+ * the GEMM.  ln_w: [K] in ln_dtype (LB_DT_F32 or LB_DT_BF16).  Replaces _Base.linear(x, W, ln=...) and its
+ * gemvq*n kernels (apsi/hub_gpu.py:1305-1315, 837-870). */
+int lb_linear_rms(int fmt, const void* x, int64_t M, int64_t K, const void* ln_w, int ln_dtype, float eps, float off,
+                  const void* codes, const void* scales, int64_t N, const void* bias, int accumulate, void* y,
+                  int64_t ldy, void* workspace, size_t ws_bytes, unsigned flags, void* stream);
+
 /* The step between a decoder's fused QKV projection and its attention: split the [B T, (nh + 2 kvh) dh] bf16
  * projection into heads; optionally RMSNorm every q / k head (qn, kn: bf16 [dh] weights, or NULL); rotate the
  * first `rot` values of every q and k head with half-split pairs [a cos - b sin, b cos + a sin] (a = v[:rot/2],
@@ -183,6 +195,7 @@ int lb_qkv_prep(const void* qkv, int B, int T, int nh, int kvh, int dh, int rot,
  * kind 0: silu g / (1 + exp(-g)); kind 1: gelu, tanh form.  Replaces hub_gpu's act_mul op
  * (apsi/hub_gpu.py:1598-1600, host form 1755-1762). */
 int lb_act_mul(const void* gu, int64_t M, int64_t I, int kind, void* out, void* stream);
+
 
 /* ---------------------------------------------------------------------------------------------- products */
 
