@@ -923,10 +923,11 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.ln_eps = ln ? ln->eps : 0.f;
   p.ln_off = ln ? ln->off : 0.f;
   // one token tile: three groups (12 warps + producer) and six ring slots; two token tiles: two groups
-  // int4: one token on the integer tensor path (half the MMAs, a third of the dequantisation work); more
-  // tokens on the bf16 path, whose n8 tile holds eight tokens
+  // int4: one or two tokens on the integer tensor path (half the MMAs, a third of the dequantisation work;
+  // [11008, 4096] at M = 2: 9.38 -> 8.78 us); more tokens on the bf16 path, whose n8 tile holds eight tokens
+  // (the integer path measured 5 % slower at M = 4 and 25-60 % slower at M = 8: heavier staging, two tiles)
   if (fmt == 2) {
-    if (M == 1) return launch_gemv_t<20, 1, 3, 1>(p, sms, 1, 6, pdl, st);
+    if (M <= 2) return launch_gemv_t<20, 1, 3, 1>(p, sms, 1, 6, pdl, st);
     // several K ranges per row (K > 4096) and more than four tokens: the ring holds four slots with two groups
     // against three with three groups once the larger activation staging is placed (measured on [4096, 11008]
     // at M = 8: 26.8 -> 21.6 us; single-range shapes are faster with three groups)
