@@ -134,8 +134,21 @@ __device__ __forceinline__ void deq_fp8_word(uint32_t w, uint32_t& q02, uint32_t
 
 // One unit (16 rows x 64 bytes of codes) against the B fragments of MT token tiles: acc += scale * (sum of
 // exact code products).  `nc` holds minus the offset correction of the thread's two tokens per tile.
+// fp4 e2m1: one word (8 codes, code 2j in the low nibble of byte j) -> the exact fp16 pairs (code 0, code 1),
+// (2, 3), (4, 5), (6, 7) through the hardware conversion.
+__device__ __forceinline__ void deq_fp4_word(uint32_t w, uint32_t (&p)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(p[0]), "=r"(p[1]), "=r"(p[2]), "=r"(p[3])
+      : "r"(w));
+}
+
 template <int FMT, int MT>
-__device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const uint32_t (&B)[MT][(FMT == 2) ? 16 : 8],
+__device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const uint32_t (&B)[MT][(FMT == 2 || FMT == 9) ? 16 : 8],
                                          const float (&nc)[MT][2], float s0, float s8, float (&acc)[MT][4]) {
   const uint32_t W0[4] = {w0.x, w0.y, w0.z, w0.w};
   const uint32_t W8[4] = {w8.x, w8.y, w8.z, w8.w};
@@ -158,6 +171,21 @@ __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const
       for (int t = 0; t < MT; ++t) {
         mma_bf16_16816_acc(c0[t], ae, B[t][4 * i + 0], B[t][4 * i + 1]);
         mma_bf16_16816_acc(c1[t], ao, B[t][4 * i + 2], B[t][4 * i + 3]);
+      }
+    }
+  } else if (FMT == 9) {
+    // fp4: natural code pairs against the activations staged in natural order (fp16, 2^-e per range)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t P0[4], P8[4];
+      deq_fp4_word(W0[i], P0);
+      deq_fp4_word(W8[i], P8);
+      const uint32_t a0[4] = {P0[0], P8[0], P0[1], P8[1]};   // codes (0,1) | (2,3)
+      const uint32_t a1[4] = {P0[2], P8[2], P0[3], P8[3]};   // codes (4,5) | (6,7)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        mma_f16_16816(c0[t], a0, B[t][4 * i + 0], B[t][4 * i + 1]);
+        mma_f16_16816(c1[t], a1, B[t][4 * i + 2], B[t][4 * i + 3]);
       }
     }
   } else {
@@ -245,7 +273,7 @@ struct GemvSmem {
 __host__ __device__ inline GemvSmem gemv_smem(int fmt, int M, int MT, int G, int xs_units, int slots, int items) {
   using namespace gemv;
   GemvSmem s;
-  const int xu = (fmt == 2 || fmt == 20) ? 256 : 128;     // staged bytes of x per unit per token
+  const int xu = (fmt == 2 || fmt == 20 || fmt == 9) ? 256 : 128;     // staged bytes of x per unit per token
   s.token_stride = xs_units * xu + 64;
   s.ring = 0;
   s.xs = slots * STAGE_BYTES;                                  // multiple of 128
@@ -276,7 +304,7 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 template <int FMT>
 __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int tok, float v) {
   if (FMT == 1) v *= __half2float(p.s16[n]);
-  if (FMT == 5 || FMT == 6) v *= reinterpret_cast<const float*>(p.s16)[n];   // fp8 rows: float32 scales
+  if (FMT == 5 || FMT == 6 || FMT == 9) v *= reinterpret_cast<const float*>(p.s16)[n];   // fp8 / fp4 rows: float32 scales
   if (p.bias) v += bf16_bits_to_f32(p.bias[n]);
   if (p.dst.n) {                            // this rank's column of every rank's output
     const uint16_t b = f32_to_bf16_bits(v);
@@ -297,9 +325,10 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
   constexpr int NCW = G * GW;                  // consumer warps
   constexpr int CT = NCW * 32;                 // consumer threads
   constexpr bool I4 = (FMT == 2 || FMT == 20);   // int4 codes (20: on the integer tensor path)
-  constexpr int XU = I4 ? 256 : 128;            // staged bytes of x per unit per token
+  constexpr bool NIB = I4 || FMT == 9;           // 4-bit codes: 128 values per 64-byte unit
+  constexpr int XU = NIB ? 256 : 128;           // staged bytes of x per unit per token
   constexpr int XCH = XU / 64;                 // 16-byte chunks of x per thread per unit
-  constexpr int KPU = I4 ? 128 : 64;            // K values per unit
+  constexpr int KPU = NIB ? 128 : 64;           // K values per unit
   constexpr int CPU = KPU / 8;                 // 16-byte chunks of x per unit
   constexpr int CPR = RANGE_UNITS * CPU;       // 16-byte chunks of x per range
   constexpr int PW = (FMT == 20) ? 2 : 4;      // partial floats per lane per token tile
@@ -332,7 +361,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t row_bytes = I4 ? p.K / 2 : p.K;
+  const int64_t row_bytes = NIB ? p.K / 2 : p.K;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < slots; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], GW); }
@@ -397,7 +426,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       };
       auto slot_of = [&](int t, int il, int jj) -> uint8_t* {
         int u, cc, vv;
-        if (I4) { u = jj >> 4; cc = (jj >> 2) & 3; vv = jj & 3; }
+        if (NIB) { u = jj >> 4; cc = (jj >> 2) & 3; vv = jj & 3; }
         else { u = jj >> 3; cc = (jj >> 1) & 3; vv = jj & 1; }
         return xs + t * L.token_stride + (il * RANGE_UNITS + u) * XU + vv * 64 + cc * 16;
       };
@@ -601,6 +630,9 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
             float g8[8];
             if (FMT == 2) {   // even class (0,4) (2,6), then odd class (1,5) (3,7)
               g8[0] = f[0]; g8[1] = f[4]; g8[2] = f[2]; g8[3] = f[6]; g8[4] = f[1]; g8[5] = f[5]; g8[6] = f[3]; g8[7] = f[7];
+            } else if (FMT == 9) {   // fp4: natural order (the code pairs of deq_fp4_word)
+#pragma unroll
+              for (int e2 = 0; e2 < 8; ++e2) g8[e2] = f[e2];
             } else {          // byte pairs (0,2) (1,3) of each word
               g8[0] = f[0]; g8[1] = f[2]; g8[2] = f[1]; g8[3] = f[3]; g8[4] = f[4]; g8[5] = f[6]; g8[6] = f[5]; g8[7] = f[7];
             }
@@ -831,7 +863,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
 // ------------------------------------------------------------------------------------------- launcher
 int gemv_max_k(int fmt) {
   // at most MAX_RANGES K ranges per row
-  return gemv::MAX_RANGES * gemv::RANGE_UNITS * gemv::UNIT * (fmt == 2 ? 2 : 1);
+  return gemv::MAX_RANGES * gemv::RANGE_UNITS * gemv::UNIT * ((fmt == 2 || fmt == 9) ? 2 : 1);
 }
 
 template <int FMT, int MT, int G, int MINB>
@@ -911,7 +943,7 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.N = N; p.K = K; p.ldy = ldy;
   p.M = static_cast<int>(M);
   p.acc = acc;
-  const int64_t row_bytes = (fmt == 2) ? K / 2 : K;
+  const int64_t row_bytes = (fmt == 2 || fmt == 9) ? K / 2 : K;
   p.total_units = static_cast<int>(row_bytes / gemv::UNIT);
   p.nblocks = static_cast<int>((N + gemv::RB - 1) / gemv::RB);
   p.nr = (p.total_units + gemv::RANGE_UNITS - 1) / gemv::RANGE_UNITS;
@@ -941,6 +973,9 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   if (fmt == 6)
     return M <= 8 ? launch_gemv_t<6, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                   : launch_gemv_t<6, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
+  if (fmt == 9)
+    return M <= 8 ? launch_gemv_t<9, 1, 3, 1>(p, sms, 1, 6, pdl, st)
+                  : launch_gemv_t<9, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
   return M <= 8 ? launch_gemv_t<1, 1, 3, 1>(p, sms, 1, 6, pdl, st)
                 : launch_gemv_t<1, 2, 2, 1>(p, sms, 1, gemv::MAX_SLOTS, pdl, st);
 }
