@@ -273,6 +273,19 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   return v;
 }
 
+// fp4 e2m1: one word (8 codes, code 2j in the low nibble of byte j) -> the exact fp16 pairs (code 0, code 1),
+// (2, 3), (4, 5), (6, 7) through the hardware conversion.
+__device__ __forceinline__ void deq_fp4_word(uint32_t w, uint32_t (&p)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(p[0]), "=r"(p[1]), "=r"(p[2]), "=r"(p[3])
+      : "r"(w));
+}
+
 // ---- RMSNorm in one fixed order, shared by the standalone norm and the norm prologue of the decode GEMV, so
 // that a fused and an unfused normalised projection give the same bits.  A row of K bf16 values is cut into
 // 16-byte chunks of 8 values; virtual thread v of 256 (eight warps of 32) adds the squares of chunks v, v + 256,

@@ -39,7 +39,7 @@ constexpr int TAIL = 512;                                  // mbarriers, TMEM ad
 // Pipeline depth: as many stages as shared memory holds (at most 8).  Narrow token tiles (small M) carry few
 // weight bytes per stage, so they need the deepest pipelines to keep enough of the weight stream in flight.
 __host__ __device__ constexpr int stages(int fmt, int bn) {
-  const int stage = bn * 128 + A_STAGE + BM * ((fmt == 2) ? 32 : 64);
+  const int stage = bn * 128 + A_STAGE + BM * ((fmt == 2 || fmt == 9) ? 32 : 64);
   const int n = (SMEM_LIMIT - 1024 - TAIL) / stage;
   return n > 8 ? 8 : n;
 }
@@ -78,7 +78,7 @@ __device__ __forceinline__ void gemm_unit(const GemmParams& p, int u, int bn, in
 
 template <int FMT>
 struct GemmCfg {
-  static constexpr int RAW_ROW = (FMT == 2) ? 32 : 64;       // code bytes of a row per stage
+  static constexpr int RAW_ROW = (FMT == 2 || FMT == 9) ? 32 : 64;   // code bytes of a row per stage
   static constexpr int RAW_STAGE = gemm::BM * RAW_ROW;
 };
 
@@ -97,6 +97,7 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits_g(float f) {
 // One warp per token row: absmax, power-of-two factor, K-permuted fp16 copy.
 // PERM 0 (int4 nibble pairs): position L of each 8-block takes x[8b + {0,4,1,5,2,6,3,7}[L]].
 // PERM 1 (int8 byte pairs):   position L of each 4-block takes x[4b + {0,2,1,3}[L]].
+// PERM 2 (fp4 code pairs):    no permutation.
 template <int PERM>
 __global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict__ x, int64_t M, int64_t K,
                                                      uint16_t* __restrict__ x16, float* __restrict__ tokscale) {
@@ -140,6 +141,9 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict_
     float g[8];
     if (PERM == 0) {
       g[0] = f[0]; g[1] = f[4]; g[2] = f[1]; g[3] = f[5]; g[4] = f[2]; g[5] = f[6]; g[6] = f[3]; g[7] = f[7];
+    } else if (PERM == 2) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) g[j] = f[j];
     } else {
       g[0] = f[0]; g[1] = f[2]; g[2] = f[1]; g[3] = f[3]; g[4] = f[4]; g[5] = f[6]; g[6] = f[5]; g[7] = f[7];
     }
@@ -189,6 +193,18 @@ __device__ __forceinline__ void deq_int8_f16(const uint4 a, const uint4 b, uint3
     const uint32_t p13 = prmt(v, 0x00006464u, 0x5341u);          // (1024 + n1, 1024 + n3)
     o[2 * i] = h2_fma(p02, 0x3C003C00u, 0xE480E480u);            // - 1152
     o[2 * i + 1] = h2_fma(p13, 0x3C003C00u, 0xE480E480u);
+  }
+}
+
+// fp4 rows: 16 bytes = 32 codes of one row -> 16 exact fp16 pairs in natural K order (pair 4i + p holds codes
+// 8i + 2p, 8i + 2p + 1), through the hardware e2m1 conversion; the row scale is applied in the epilogue.
+__device__ __forceinline__ void deq_fp4_f16(const uint4 raw, uint32_t (&o)[16]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t p[4];
+    deq_fp4_word(w[i], p);
+    o[4 * i] = p[0]; o[4 * i + 1] = p[1]; o[4 * i + 2] = p[2]; o[4 * i + 3] = p[3];
   }
 }
 
@@ -366,10 +382,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);   // MMA done with A
         uint32_t o[16];
         const uint32_t rbase = smem_u32(raw + slot * Cfg::RAW_STAGE) + rloc * Cfg::RAW_ROW;
-        if (FMT == 2) {
+        if (FMT == 2 || FMT == 9) {
           // SWIZZLE_32B: 16-byte chunk index ^= bit 7 of the offset (row >> 2)
           const uint4 r = lds_v4(rbase + 16 * (h ^ ((rloc >> 2) & 1)));
-          deq_int4_f16(r, s2, o);
+          if (FMT == 2) deq_int4_f16(r, s2, o);
+          else deq_fp4_f16(r, o);
         } else {
           // SWIZZLE_64B: chunk index (0..3) ^= bits 7..8 of the offset (row >> 1)
           const int sw = (rloc >> 1) & 3;
@@ -408,7 +425,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       tc_fence_after();
       float rs = 1.f, bias = 0.f;
       if (FMT == 1) rs = __half2float(p.s16[rowc]);
-      if (FMT == 5 || FMT == 6) rs = reinterpret_cast<const float*>(p.s16)[rowc];   // fp8 rows: float32 scales
+      if (FMT == 5 || FMT == 6 || FMT == 9) rs = reinterpret_cast<const float*>(p.s16)[rowc];   // fp8 / fp4 rows: float32 scales
       if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
       const bool row_ok = row < p.N;
 #pragma unroll 1
@@ -468,7 +485,7 @@ static PFN_encodeTiled get_encode() {
 static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
 
 size_t gemm_smem_bytes(int fmt, int bn) {
-  const int raw = (fmt == 2) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
+  const int raw = (fmt == 2 || fmt == 9) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
   return 1024 + static_cast<size_t>(gemm::stages(fmt, bn)) * (bn * 128 + gemm::A_STAGE + raw) + gemm::TAIL;
 }
 
@@ -513,6 +530,8 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
     if (fmt == 2)
       prep_x_kernel<0><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
+    else if (fmt == 9)
+      prep_x_kernel<2><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
     else
       prep_x_kernel<1><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
     cudaError_t e = cudaGetLastError();
@@ -534,15 +553,16 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     }
   }
   {
-    const int64_t row_bytes = (fmt == 2) ? K / 2 : K;
-    const cuuint32_t raw_row = (fmt == 2) ? GemmCfg<2>::RAW_ROW : GemmCfg<1>::RAW_ROW;
+    const bool nib = (fmt == 2 || fmt == 9);          // 4-bit codes
+    const int64_t row_bytes = nib ? K / 2 : K;
+    const cuuint32_t raw_row = nib ? GemmCfg<2>::RAW_ROW : GemmCfg<1>::RAW_ROW;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
     cuuint32_t box[2] = {raw_row, static_cast<cuuint32_t>(gemm::BM)};
     cuuint32_t es[2] = {1, 1};
     CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(codes), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     fmt == 2 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     nib ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       *why = "cuTensorMapEncodeTiled failed for the weight codes";
@@ -602,6 +622,16 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, txs, p, sms, st);
     if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, txs, p, sms, st);
     return launch_gemm_t<2, 256, false>(tx, tw, txs, p, sms, st);
+  }
+  if (fmt == 9) {
+    if (p.dst.n) {
+      if (BN == 64) return launch_gemm_t<9, 64, true>(tx, tw, txs, p, sms, st);
+      if (BN == 128) return launch_gemm_t<9, 128, true>(tx, tw, txs, p, sms, st);
+      return launch_gemm_t<9, 256, true>(tx, tw, txs, p, sms, st);
+    }
+    if (BN == 64) return launch_gemm_t<9, 64, false>(tx, tw, txs, p, sms, st);
+    if (BN == 128) return launch_gemm_t<9, 128, false>(tx, tw, txs, p, sms, st);
+    return launch_gemm_t<9, 256, false>(tx, tw, txs, p, sms, st);
   }
   if (fmt == 5 || fmt == 6) {
     if (p.dst.n) {

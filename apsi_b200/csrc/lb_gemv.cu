@@ -134,19 +134,6 @@ __device__ __forceinline__ void deq_fp8_word(uint32_t w, uint32_t& q02, uint32_t
 
 // One unit (16 rows x 64 bytes of codes) against the B fragments of MT token tiles: acc += scale * (sum of
 // exact code products).  `nc` holds minus the offset correction of the thread's two tokens per tile.
-// fp4 e2m1: one word (8 codes, code 2j in the low nibble of byte j) -> the exact fp16 pairs (code 0, code 1),
-// (2, 3), (4, 5), (6, 7) through the hardware conversion.
-__device__ __forceinline__ void deq_fp4_word(uint32_t w, uint32_t (&p)[4]) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(p[0]), "=r"(p[1]), "=r"(p[2]), "=r"(p[3])
-      : "r"(w));
-}
-
 template <int FMT, int MT>
 __device__ __forceinline__ void unit_mma(const uint4& w0, const uint4& w8, const uint32_t (&B)[MT][(FMT == 2 || FMT == 9) ? 16 : 8],
                                          const float (&nc)[MT][2], float s0, float s8, float (&acc)[MT][4]) {

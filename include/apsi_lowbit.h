@@ -211,9 +211,8 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
  * `workspace` (lb_linear_workspace_size() bytes, 256-byte aligned, contents need no initialisation).
  * x, codes and scales must be 16-byte aligned.  Formats: INT8_ROW and INT4_G128 (binary16 scales), FP8_E4M3
  * and FP8_E5M2 rows (codes uint8 [N, K], float32 scales [N]: the codes become exact fp16 operands), FP4_E2M1
- * rows for M <= 16 only (codes [N, K/2] as lb_quant_minifloat packs them, K % 128 == 0, float32 scales [N];
- * the codes become exact fp16 operands through the hardware e2m1 conversion); the other formats, and FP4_E2M1
- * with M > 16, return LB_E_UNSUPPORTED.
+ * rows (codes [N, K/2] as lb_quant_minifloat packs them, K % 128 == 0, float32 scales [N]; the codes become
+ * exact fp16 operands through the hardware e2m1 conversion); the other formats return LB_E_UNSUPPORTED.
  * Replaces precision.qmatmul / models.qlinear (apsi/precision.py:294-299, apsi/models.py:302-308) and
  * _Base.linear -> Runner.gemv / Runner.gemm with bias and acc (apsi/hub_gpu.py:1305-1315, 1491-1528). */
 int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,

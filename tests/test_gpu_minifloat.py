@@ -102,11 +102,12 @@ def test_fp8_fused_product_matches_oracle(cuda, name, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 11008, 4096), (5, 300, 1024), (8, 4096, 11008),
-                                   (16, 520, 2048), (12, 1000, 16384), (64, 1000, 512)])
+                                   (16, 520, 2048), (12, 1000, 16384), (64, 1000, 512), (17, 300, 1024),
+                                   (300, 768, 1024), (2048, 1024, 2048)])
 def test_fp4_fused_product_matches_oracle(cuda, M, N, K):
     """Per-row fp4 e2m1 weights: the fused decode GEMV for M <= 16 (codes to exact fp16 through the hardware
-    e2m1 conversion; one K range and the cluster split over several), the dequantise-then-GEMM path above, both
-    against the float64 product of the oracle's dequantised weights with the layer tolerance."""
+    e2m1 conversion; one K range and the cluster split over several), the tcgen05 GEMM above, both against the
+    float64 product of the oracle's dequantised weights with the layer tolerance."""
     import torch
     from apsi_b200 import precision as P
     rng = np.random.default_rng(M * 7 + N + K)
@@ -122,24 +123,29 @@ def test_fp4_fused_product_matches_oracle(cuda, M, N, K):
     assert O.rel_frobenius(y, ref) <= 2e-3
 
 
-def test_fp4_through_the_c_abi_and_its_limits(cuda):
-    """lb_linear with LB_FMT_FP4_E2M1 codes straight from lb_quant_minifloat; M > 16 is LB_E_UNSUPPORTED."""
+def test_fp4_through_the_c_abi(cuda):
+    """lb_linear with LB_FMT_FP4_E2M1 codes straight from lb_quant_minifloat, on the GEMV and on the GEMM, and
+    the GEMM's column shards bit-identical to the full product."""
     import torch
     from apsi_b200 import kernels as K
-    from apsi_b200._lib import FMT_FP4_E2M1, LB_E_UNSUPPORTED, LowbitError
+    from apsi_b200._lib import FMT_FP4_E2M1
     g = torch.Generator(device=cuda)
     g.manual_seed(4)
     N, Kd = 640, 2048
     W = torch.randn((N, Kd), generator=g, device=cuda) * 0.03
     codes, s32 = K.quant_minifloat(W, FMT_FP4_E2M1, True)
-    x = torch.randn((4, Kd), generator=g, device=cuda).to(torch.bfloat16)
-    y = K.linear(FMT_FP4_E2M1, x, codes, s32, N).float()
     Wd = K.dequant_minifloat(FMT_FP4_E2M1, codes, N, Kd, s32)
-    ref = x.float() @ Wd.t()
-    assert float((y - ref).abs().max()) <= 1e-2 * float(ref.abs().max())
-    with pytest.raises(LowbitError) as e:
-        K.linear(FMT_FP4_E2M1, torch.zeros((17, Kd), dtype=torch.bfloat16, device=cuda), codes, s32, N)
-    assert e.value.code == LB_E_UNSUPPORTED
+    for M in (4, 100):
+        x = torch.randn((M, Kd), generator=g, device=cuda).to(torch.bfloat16)
+        y = K.linear(FMT_FP4_E2M1, x, codes, s32, N)
+        ref = x.float() @ Wd.t()
+        assert float((y.float() - ref).abs().max()) <= 1e-2 * float(ref.abs().max())
+        half = N // 2
+        cv = codes.view(N, Kd // 2)
+        for r in range(2):
+            part = K.linear(FMT_FP4_E2M1, x, cv[r * half:(r + 1) * half].contiguous(),
+                            s32[r * half:(r + 1) * half].contiguous(), half)
+            assert torch.equal(part, y[:, r * half:(r + 1) * half])
 
 
 @pytest.mark.parametrize("name", ["fp8_e4m3", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1"])
