@@ -288,18 +288,20 @@ int lb_gguf_decode(int kind, const uint8_t* blocks, int64_t n, float* out, void*
 
 static bool use_gemv(int64_t M) { return M <= 16; }
 
-// formats with a fused product: int8 rows, int4 groups of 128, fp8 e4m3 / e5m2 and fp4 e2m1 rows (float32 row
-// scales)
+// formats with a fused product: int8 rows, int4 groups of 128, fp8 e4m3 / e5m2, fp6 e3m2 / e2m3 and fp4 e2m1
+// rows (float32 row scales); fp6 has the decode product only (M <= 16)
 static bool has_product(int fmt) {
-  return fmt == LB_FMT_INT8_ROW || fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP8_E4M3 || fmt == LB_FMT_FP8_E5M2 ||
-         fmt == LB_FMT_FP4_E2M1;
+  return fmt == LB_FMT_INT8_ROW || fmt == LB_FMT_INT4_G128 || (fmt >= LB_FMT_FP8_E4M3 && fmt <= LB_FMT_FP4_E2M1);
 }
+static bool is_fp6(int fmt) { return fmt == LB_FMT_FP6_E3M2 || fmt == LB_FMT_FP6_E2M3; }
 
 int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* bytes) {
   if (!bytes) return fail(LB_E_ARG, "lb_linear_workspace_size: bytes is NULL");
   if (!has_product(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_workspace_size: sizes must be positive");
+  if (!use_gemv(M) && is_fp6(fmt))
+    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 formats have a product for M <= 16 only");
   *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
   return LB_OK;
 }
@@ -314,8 +316,10 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void*
   if (!x || !codes || !scales || !y) return fail(LB_E_ARG, "lb_linear: x, codes, scales and y are required");
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear: M, N, K must be positive");
   if (M > (1LL << 31) || N > (1LL << 31)) return fail(LB_E_ARG, "lb_linear: M and N must be below 2^31");
-  const int64_t kmult = (fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP4_E2M1) ? 128 : 64;
+  const int64_t kmult = (fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP4_E2M1) ? 128 : (is_fp6(fmt) ? 16 : 64);
   if (K % kmult) return fail(LB_E_ARG, "lb_linear: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
+  if (!use_gemv(M) && is_fp6(fmt))
+    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 formats have a product for M <= 16 only");
   if (ldy < N) return fail(LB_E_ARG, "lb_linear: ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
   if (!aligned(x, 16) || !aligned(codes, 16) || !aligned(scales, 16))
     return fail(LB_E_ALIGN, "lb_linear: x, codes and scales must be 16-byte aligned");
@@ -369,6 +373,7 @@ int lb_linear_rms(int fmt, const void* x, int64_t M, int64_t K, const void* ln_w
                   const void* codes, const void* scales, int64_t N, const void* bias, int accumulate, void* y,
                   int64_t ldy, void* workspace, size_t ws_bytes, unsigned flags, void* stream) {
   if (!ln_w) return fail(LB_E_ARG, "lb_linear_rms: ln_w is required");
+  if (is_fp6(fmt)) return fail(LB_E_UNSUPPORTED, "lb_linear_rms: fp6 formats have no normalised product");
   if (ln_dtype != LB_DT_F32 && ln_dtype != LB_DT_BF16) return fail(LB_E_ARG, "lb_linear_rms: ln_dtype must be F32 or BF16");
   if (!aligned(ln_w, ln_dtype == LB_DT_F32 ? 4 : 2)) return fail(LB_E_ALIGN, "lb_linear_rms: ln_w must be element aligned");
   if (use_gemv(M)) {

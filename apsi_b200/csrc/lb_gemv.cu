@@ -291,7 +291,7 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 template <int FMT>
 __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int tok, float v) {
   if (FMT == 1) v *= __half2float(p.s16[n]);
-  if (FMT == 5 || FMT == 6 || FMT == 9) v *= reinterpret_cast<const float*>(p.s16)[n];   // fp8 / fp4 rows: float32 scales
+  if (FMT >= 5 && FMT <= 9) v *= reinterpret_cast<const float*>(p.s16)[n];   // minifloat rows: float32 scales
   if (p.bias) v += bf16_bits_to_f32(p.bias[n]);
   if (p.dst.n) {                            // this rank's column of every rank's output
     const uint16_t b = f32_to_bf16_bits(v);
@@ -847,8 +847,95 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
   }
 }
 
+// ------------------------------------------------------------------------------------------- fp6 rows
+// fp6 e3m2 (FMT 7) / e2m3 (FMT 8) rows, M <= 16: four codes per three bytes (value j of a group at bits
+// 6j .. 6j + 5 of its little-endian 24-bit word) do not fit the 64-byte units of gemv_kernel, so this product
+// runs on the CUDA cores.  One warp per row at a time; lane l takes the 12-byte chunks l, l + 32, ... of the
+// row (16 values each), turns each pair of codes into an exact fp16 pair with the hardware conversion and
+// accumulates value * x in float32 per token in chunk order; the lanes are added by the xor butterfly (a fixed
+// order, so every launch and every column shard gives the same bits); the epilogue is gemv_kernel's.
+template <int FMT>
+__device__ __forceinline__ void deq_fp6_group(uint32_t g, float (&v)[4]) {
+  // the four 6-bit fields into the low bits of four bytes
+  const uint32_t u = (g & 0x3Fu) | ((g << 2) & 0x3F00u) | ((g << 4) & 0x3F0000u) | ((g << 6) & 0x3F000000u);
+  uint32_t lo, hi;
+  if (FMT == 7) {
+    asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e3m2x2 %0, a;\n\t}" : "=r"(lo) : "r"(u));
+    asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e3m2x2 %0, a;\n\t}" : "=r"(hi) : "r"(u >> 16));
+  } else {
+    asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e2m3x2 %0, a;\n\t}" : "=r"(lo) : "r"(u));
+    asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e2m3x2 %0, a;\n\t}" : "=r"(hi) : "r"(u >> 16));
+  }
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) gemv_fp6_kernel(const GemvParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t rb = p.K / 4 * 3;            // code bytes of a row
+  const int64_t nch = p.K / 16;              // 12-byte chunks of a row
+  for (int64_t n = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); n < p.N; n += warps) {
+    float acc[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+    const uint8_t* wr = p.w + n * rb;
+    for (int64_t c = lane; c < nch; c += 32) {
+      const uint8_t* q = wr + 12 * c;        // 4-byte aligned: rows start at multiples of 12 bytes
+      const uint32_t w0 = ldg_nc_u32(q), w1 = ldg_nc_u32(q + 4), w2 = ldg_nc_u32(q + 8);
+      float v[16];
+      {
+        float g4[4];
+        deq_fp6_group<FMT>(w0 & 0xFFFFFFu, g4);
+        v[0] = g4[0]; v[1] = g4[1]; v[2] = g4[2]; v[3] = g4[3];
+        deq_fp6_group<FMT>((w0 >> 24) | ((w1 & 0xFFFFu) << 8), g4);
+        v[4] = g4[0]; v[5] = g4[1]; v[6] = g4[2]; v[7] = g4[3];
+        deq_fp6_group<FMT>((w1 >> 16) | ((w2 & 0xFFu) << 16), g4);
+        v[8] = g4[0]; v[9] = g4[1]; v[10] = g4[2]; v[11] = g4[3];
+        deq_fp6_group<FMT>(w2 >> 8, g4);
+        v[12] = g4[0]; v[13] = g4[1]; v[14] = g4[2]; v[15] = g4[3];
+      }
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        if (t < p.M) {
+          const uint16_t* xr = p.x + static_cast<int64_t>(t) * p.K + 16 * c;
+          const uint4 a = ldg_nc_v4(xr), b = ldg_nc_v4(xr + 8);
+          const uint32_t r[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          float s = acc[t];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            s = fmaf(v[2 * e], __uint_as_float(r[e] << 16), s);
+            s = fmaf(v[2 * e + 1], __uint_as_float(r[e] & 0xFFFF0000u), s);
+          }
+          acc[t] = s;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      if (t < p.M) {
+        float s = acc[t];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == t) store_out<FMT>(p, n, t, s);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------- launcher
 int gemv_max_k(int fmt) {
+  if (fmt == 7 || fmt == 8) return 1 << 30;   // the fp6 product has no K ranges
   // at most MAX_RANGES K ranges per row
   return gemv::MAX_RANGES * gemv::RANGE_UNITS * gemv::UNIT * ((fmt == 2 || fmt == 9) ? 2 : 1);
 }
@@ -941,6 +1028,21 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.ln_vec = (ln && (reinterpret_cast<uintptr_t>(ln->w) & 15) == 0) ? 1 : 0;
   p.ln_eps = ln ? ln->eps : 0.f;
   p.ln_off = ln ? ln->off : 0.f;
+  if (fmt == 7 || fmt == 8) {
+    if (ln) return cudaErrorNotSupported;     // the norm prologue lives in gemv_kernel's staging
+    const int64_t want = (N + 7) / 8;         // one warp per row
+    const unsigned grid = static_cast<unsigned>(want < 4LL * sms ? want : 4LL * sms);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return fmt == 7 ? cudaLaunchKernelEx(&cfg, gemv_fp6_kernel<7>, p) : cudaLaunchKernelEx(&cfg, gemv_fp6_kernel<8>, p);
+  }
   // one token tile: three groups (12 warps + producer) and six ring slots; two token tiles: two groups
   // int4: one or two tokens on the integer tensor path (half the MMAs, a third of the dequantisation work;
   // [11008, 4096] at M = 2: 9.38 -> 8.78 us); more tokens on the bf16 path, whose n8 tile holds eight tokens

@@ -49,9 +49,11 @@ int scratch_for_device(int dev, void** out) {
 extern "C" int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                                  int64_t N, const void* bias, int accumulate, void* y, int64_t ldy, void* stream) {
   using namespace lb;
+  const bool fp6 = (fmt == LB_FMT_FP6_E3M2 || fmt == LB_FMT_FP6_E2M3);
   if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128 && fmt != LB_FMT_FP8_E4M3 && fmt != LB_FMT_FP8_E5M2 &&
-      fmt != LB_FMT_FP4_E2M1)
-    return fail(LB_E_UNSUPPORTED, "lb_linear_noalloc: format %d has no product kernel in this build", fmt);
+      fmt != LB_FMT_FP4_E2M1 && !(fp6 && M <= 16))
+    return fail(LB_E_UNSUPPORTED, "lb_linear_noalloc: format %d has no product kernel for M = %lld in this build", fmt,
+                (long long)M);
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_noalloc: M, N, K must be positive");
   if (M > (1LL << 31) || K > (1LL << 31)) return fail(LB_E_ARG, "lb_linear_noalloc: M and K must be below 2^31");
   if (M <= 16)   // decode path: no scratch at all

@@ -212,7 +212,9 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
  * x, codes and scales must be 16-byte aligned.  Formats: INT8_ROW and INT4_G128 (binary16 scales), FP8_E4M3
  * and FP8_E5M2 rows (codes uint8 [N, K], float32 scales [N]: the codes become exact fp16 operands), FP4_E2M1
  * rows (codes [N, K/2] as lb_quant_minifloat packs them, K % 128 == 0, float32 scales [N]; the codes become
- * exact fp16 operands through the hardware e2m1 conversion); the other formats return LB_E_UNSUPPORTED.
+ * exact fp16 operands through the hardware e2m1 conversion), FP6_E3M2 and FP6_E2M3 rows for M <= 16 only
+ * (codes [N, 3K/4] as lb_quant_minifloat packs them, K % 16 == 0, float32 scales [N]; a CUDA-core product, the
+ * codes exact in fp16); the other formats, and fp6 with M > 16, return LB_E_UNSUPPORTED.
  * Replaces precision.qmatmul / models.qlinear (apsi/precision.py:294-299, apsi/models.py:302-308) and
  * _Base.linear -> Runner.gemv / Runner.gemm with bias and acc (apsi/hub_gpu.py:1305-1315, 1491-1528). */
 int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales, int64_t N,

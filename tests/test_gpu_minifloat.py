@@ -148,6 +148,62 @@ def test_fp4_through_the_c_abi(cuda):
             assert torch.equal(part, y[:, r * half:(r + 1) * half])
 
 
+@pytest.mark.parametrize("name", ["fp6_e3m2", "fp6_e2m3"])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 300, 1040), (8, 1000, 11008), (16, 520, 2048),
+                                   (1, 77, 16), (64, 300, 512)])
+def test_fp6_fused_product_matches_oracle(cuda, name, M, N, K):
+    """Per-row fp6 weights: the fused decode product for M <= 16 (four codes per three bytes, exact fp16
+    through the hardware conversion, float32 accumulation on the CUDA cores), dequantise-then-GEMM above; both
+    against the float64 product of the oracle's dequantised weights with the layer tolerance."""
+    import torch
+    from apsi_b200 import precision as P
+    rng = np.random.default_rng(M * 5 + N + K)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    q = P.quantize(W, name, axis=0)
+    codes, s = O.quant_minifloat(W, name, 0)
+    Wd = O.dequant_minifloat(codes, name, (N, K), s).astype(np.float64)
+    xb = O.bf16_round(x)
+    ref = xb.astype(np.float64) @ Wd.T
+    y = P.qmatmul(torch.from_numpy(xb).to(cuda).to(torch.bfloat16), q).float().cpu().numpy()
+    assert O.max_abs_ratio(y, ref) <= 1e-2
+    assert O.rel_frobenius(y, ref) <= 2e-3
+
+
+@pytest.mark.parametrize("name", ["fp6_e3m2", "fp6_e2m3"])
+def test_fp6_through_the_c_abi(cuda, name):
+    """lb_linear on fp6 codes straight from lb_quant_minifloat, with bias and accumulation; column shards are
+    bit-identical to the full product; repeated calls give the same bits; M > 16 is LB_E_UNSUPPORTED."""
+    import torch
+    from apsi_b200 import kernels as K
+    from apsi_b200._lib import MINIFLOAT_FMT, LB_E_UNSUPPORTED, LowbitError
+    f = MINIFLOAT_FMT[name]
+    g = torch.Generator(device=cuda)
+    g.manual_seed(8)
+    N, Kd, M = 640, 2048, 5
+    W = torch.randn((N, Kd), generator=g, device=cuda) * 0.03
+    codes, s32 = K.quant_minifloat(W, f, True)
+    Wd = K.dequant_minifloat(f, codes, N, Kd, s32)
+    x = torch.randn((M, Kd), generator=g, device=cuda).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g, device=cuda).to(torch.bfloat16)
+    y0 = torch.randn((M, N), generator=g, device=cuda).to(torch.bfloat16)
+    y = K.linear(f, x, codes, s32, N, bias=bias, out=y0.clone(), accumulate=True)
+    ref = x.float() @ Wd.t() + bias.float() + y0.float()
+    assert float((y.float() - ref).abs().max()) <= 1e-2 * float(ref.abs().max())
+    full = K.linear(f, x, codes, s32, N)
+    assert torch.equal(full, K.linear(f, x, codes, s32, N))
+    rb = Kd // 4 * 3
+    cv = codes.view(N, rb)
+    half = N // 2
+    for r in range(2):
+        part = K.linear(f, x, cv[r * half:(r + 1) * half].contiguous(), s32[r * half:(r + 1) * half].contiguous(),
+                        half)
+        assert torch.equal(part, full[:, r * half:(r + 1) * half])
+    with pytest.raises(LowbitError) as e:
+        K.linear(f, torch.zeros((17, Kd), dtype=torch.bfloat16, device=cuda), codes, s32, N)
+    assert e.value.code == LB_E_UNSUPPORTED
+
+
 @pytest.mark.parametrize("name", ["fp8_e4m3", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1"])
 def test_tensor_scaled_and_packed_products(cuda, name):
     """axis=None weights and the fp6 / fp4 formats: same tolerance against the oracle's product."""

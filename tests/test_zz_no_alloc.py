@@ -24,7 +24,9 @@ def test_noalloc_rejects_shapes_beyond_the_scratch(lib):
     rc = lib.lb_linear_noalloc(_lib.FMT_INT4_G128, fake, M, K, fake, fake, 256, null, 0, fake, 256, null)
     assert rc == _lib.LB_E_WORKSPACE
     assert b"scratch" in lib.lb_last_error()
-    rc = lib.lb_linear_noalloc(7, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null)    # fp6: no product
+    rc = lib.lb_linear_noalloc(3, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null)    # g32: no product
+    assert rc == _lib.LB_E_UNSUPPORTED
+    rc = lib.lb_linear_noalloc(7, fake, 17, 128, fake, fake, 4, null, 0, fake, 4, null)   # fp6: decode only
     assert rc == _lib.LB_E_UNSUPPORTED
 
 
