@@ -1,7 +1,7 @@
 """Write the golden vectors that pin the oracle and the kernels to the reference.
 
-Run in a container where the reference is importable (its ``apsi`` package on ``APSI_REF`` or
-``/root/reference``):
+Run where the reference is importable (``APSI_REF`` names the directory that holds its ``apsi`` package;
+without it, the reference checkout of the build container is used):
 
     python tests/golden/make_golden.py
 
