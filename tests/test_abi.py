@@ -108,3 +108,12 @@ def test_python_layer_raises_loudly_without_a_device():
         pytest.skip("a device is present")
     with pytest.raises(_lib.LowbitError):
         kernels.quant_int4_g128(torch.zeros(4, 128))
+    x = torch.zeros(2, 128, dtype=torch.bfloat16)
+    codes, s16 = torch.zeros(4, 64, dtype=torch.uint8), torch.zeros(4, 1, dtype=torch.float16)
+    for call in (lambda: kernels.linear(_lib.FMT_INT4_G128, x, codes, s16, 4),
+                 lambda: kernels.linear(_lib.FMT_FP4_E2M1, x, codes, torch.zeros(4), 4),
+                 lambda: kernels.linear_rms(_lib.FMT_INT4_G128, x, torch.ones(128), codes, s16, 4),
+                 lambda: kernels.rmsnorm(x, torch.ones(128)),
+                 lambda: kernels.act_mul(torch.zeros(2, 256, dtype=torch.bfloat16), 128)):
+        with pytest.raises(_lib.LowbitError):      # host tensors: refused, never computed on the CPU
+            call()
