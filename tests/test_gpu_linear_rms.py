@@ -20,8 +20,13 @@ def _weights(torch, cuda, N, K, fmt, seed):
     if fmt == "int4":
         codes, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
         return FMT_INT4_G128, codes, s16
-    codes, s16, _ = Kn.quant_int8_rows(W, want_scale32=False)
-    return FMT_INT8_ROW, codes, s16
+    if fmt == "int8":
+        codes, s16, _ = Kn.quant_int8_rows(W, want_scale32=False)
+        return FMT_INT8_ROW, codes, s16
+    from apsi_b200._lib import MINIFLOAT_FMT       # fp8 / fp4 rows: float32 row scales
+    f = MINIFLOAT_FMT[fmt]
+    codes, s32 = Kn.quant_minifloat(W, f, True)
+    return f, codes, s32
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 11008, 4096), (8, 6144, 4096), (8, 22016, 4096), (3, 520, 1024),
@@ -44,6 +49,25 @@ def test_fused_norm_is_bit_identical_to_norm_then_linear(cuda, M, N, K, fmt, ln_
         torch.cuda.synchronize()
         assert Kn.device_errors() == 0
         assert torch.equal(got, ref), (eps, off)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (8, 1000, 2048), (5, 640, 11008), (40, 520, 2048)])
+@pytest.mark.parametrize("fmt", ["fp8_e4m3", "fp8_e5m2", "fp4_e2m1"])
+def test_fused_norm_on_minifloat_rows(cuda, M, N, K, fmt):
+    """The norm prologue on the fp16-staged formats (fp8, fp4 rows): the same bits as the norm followed by the
+    product, on the GEMV (one K range and several) and on the GEMM."""
+    import torch
+    from apsi_b200 import kernels as Kn
+    f, codes, sc = _weights(torch, cuda, N, K, fmt, seed=M * 3 + N + K)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(M + 2 * K)
+    x = (torch.randn((M, K), generator=g, device=cuda) * 2.0).to(torch.bfloat16)
+    ln = (torch.randn(K, generator=g, device=cuda) * 0.2 + 1.0).to(torch.bfloat16)
+    ref = Kn.linear(f, Kn.rmsnorm(x, ln, eps=1e-5, off=0.5), codes, sc, N)
+    got = Kn.linear_rms(f, x, ln, codes, sc, N, eps=1e-5, off=0.5)
+    torch.cuda.synchronize()
+    assert Kn.device_errors() == 0
+    assert torch.equal(got, ref)
 
 
 def test_fused_norm_with_bias_accumulate_static_and_unaligned_weights(cuda):
