@@ -604,7 +604,9 @@ def run_case(case):
     gemv_down int4-g128 GEMV, M=1, [4096, 11008] (K split over a 2-CTA cluster), 12 launches
     gemv_m16  int4-g128 GEMV, M=16, [11008, 4096], 12 launches
     gemm      int4-g128 GEMM, M=2048, [12288, 4096], 4 launches (each also runs prep_x_kernel)
-    quant     int4-g128 quantisation of a float32 [11008, 4096] weight, 4 launches"""
+    quant     int4-g128 quantisation of a float32 [11008, 4096] weight, 4 launches
+    decode_step  one eager decode step of the configs[3] decoder (batch 8 after a 512-token prefill), inside
+              the NVTX range "decode_step" (capture it with ncu --nvtx --nvtx-include "decode_step/")"""
     import torch
     from apsi_b200 import kernels as Kn
     from apsi_b200._lib import FMT_INT4_G128
@@ -634,6 +636,19 @@ def run_case(case):
         W = torch.randn((N1, K1), generator=gen, device=dev) * 0.02
         for _ in range(4):
             Kn.quant_int4_g128(W, want_scale32=True)
+    elif case == "decode_step":
+        from apsi_b200.decoder import QuantDecoder, DecoderConfig
+        cfg = DecoderConfig()
+        model = QuantDecoder(cfg, device=dev, fmt="int4", seed=0)
+        ids = torch.randint(0, cfg.V, (8, 512), device=dev, generator=gen)
+        cache = model.new_cache(8, 520)
+        tok = model.prefill(ids, cache).float().argmax(-1)
+        pos = torch.full((1,), 512, dtype=torch.int64, device=dev)
+        model.decode_step(tok, cache, pos)                   # first use of every kernel shape
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_push("decode_step")
+        model.decode_step(tok, cache, pos)
+        torch.cuda.nvtx.range_pop()
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize(dev)
