@@ -11,8 +11,8 @@ apsi/hub_models.py:1018-1092), one block per layer:
     X   += linear(down, silu(G) * U)                                     (act_mul, down projection)
     logits = linear(head, X_last, ln=final_norm)
 
-All projections -- QKV, O, gate/up, down and the LM head -- are int4 group-128 (or int8 per-row) weights in
-the library's packed layout, multiplied by ``kernels.linear``: the decode GEMV for up to 16 rows, the tcgen05
+All projections -- QKV, O, gate/up, down and the LM head -- are int4 group-128 (or int8, fp8 e4m3 or fp4 e2m1
+per-row) weights in the library's packed layout, multiplied by ``kernels.linear``: the decode GEMV for up to 16 rows, the tcgen05
 GEMM above; the residual adds are the kernels' accumulate epilogue.  The normalised projections (QKV,
 gate/up, head) go through ``kernels.linear_rms``: for decode the RMSNorm runs inside the GEMV's activation
 staging, for prefill ``lb_rmsnorm`` precedes the GEMM (the same bits either way).  The QKV split with rotary
@@ -32,7 +32,7 @@ import torch
 import torch.nn.functional as F
 
 from . import kernels as Kn
-from ._lib import FMT_INT4_G128, FMT_INT8_ROW, LowbitError, LB_E_ARG
+from ._lib import FMT_INT4_G128, FMT_INT8_ROW, FMT_FP8_E4M3, FMT_FP4_E2M1, LowbitError, LB_E_ARG
 
 __all__ = ["DecoderConfig", "QuantDecoder", "KVCache"]
 
@@ -71,8 +71,10 @@ class _Proj:
         self.fmt = fmt
         if fmt == FMT_INT4_G128:
             self.codes, self.scales, _ = Kn.quant_int4_g128(W, want_scale32=False)
-        else:
+        elif fmt == FMT_INT8_ROW:
             self.codes, self.scales, _ = Kn.quant_int8_rows(W, want_scale32=False)
+        else:                                    # fp8 / fp4 rows: float32 row scales
+            self.codes, self.scales = Kn.quant_minifloat(W, fmt, True)
 
     def __call__(self, x, out=None, accumulate=False, static=False, ln=None, eps=1e-6):
         if ln is not None:                       # RMSNorm prologue (inside the decode GEMV for M <= 16)
@@ -82,7 +84,9 @@ class _Proj:
                          static_weights=static)
 
     def dequantized(self):
-        return Kn.dequant(self.fmt, self.codes, self.scales, self.N, self.K)
+        if self.fmt in (FMT_INT4_G128, FMT_INT8_ROW):
+            return Kn.dequant(self.fmt, self.codes, self.scales, self.N, self.K)
+        return Kn.dequant_minifloat(self.fmt, self.codes, self.N, self.K, self.scales)
 
 
 class QuantDecoder:
@@ -91,9 +95,10 @@ class QuantDecoder:
     def __init__(self, cfg=None, device="cuda", fmt="int4", seed=0, max_positions=8192):
         self.cfg = cfg = cfg or DecoderConfig()
         self.dev = torch.device(device)
-        if fmt not in ("int4", "int8"):
-            raise LowbitError(LB_E_ARG, f"projection format '{fmt}' is not int4 or int8")
-        self.fmt = FMT_INT4_G128 if fmt == "int4" else FMT_INT8_ROW
+        fmts = {"int4": FMT_INT4_G128, "int8": FMT_INT8_ROW, "fp8_e4m3": FMT_FP8_E4M3, "fp4_e2m1": FMT_FP4_E2M1}
+        if fmt not in fmts:
+            raise LowbitError(LB_E_ARG, f"projection format '{fmt}' is not one of {sorted(fmts)}")
+        self.fmt = fmts[fmt]
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
         width = (cfg.nh + 2 * cfg.kvh) * cfg.dh
@@ -125,9 +130,9 @@ class QuantDecoder:
 
     # ------------------------------------------------------------------ pieces
     def weight_bytes(self):
-        n = sum(p.codes.numel() + 2 * p.scales.numel() for Ld in self.layers for p in
-                (Ld["qkv"], Ld["o"], Ld["gu"], Ld["down"]))
-        return n + self.head.codes.numel() + 2 * self.head.scales.numel()
+        def nb(p):
+            return p.codes.numel() * p.codes.element_size() + p.scales.numel() * p.scales.element_size()
+        return sum(nb(p) for Ld in self.layers for p in (Ld["qkv"], Ld["o"], Ld["gu"], Ld["down"])) + nb(self.head)
 
     def new_cache(self, batch, cap):
         if cap > self.max_positions:

@@ -52,7 +52,7 @@ def _reference_logits(model, ids):
     return rms(X[:, -1], model.norm) @ model.head.dequantized().T
 
 
-@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("fmt", ["int4", "int8", "fp8_e4m3", "fp4_e2m1"])
 def test_prefill_matches_float32_restatement(cuda, fmt):
     from apsi_b200.decoder import QuantDecoder, DecoderConfig
     model = QuantDecoder(DecoderConfig(**SMALL), device=cuda, fmt=fmt, seed=3)
@@ -64,10 +64,11 @@ def test_prefill_matches_float32_restatement(cuda, fmt):
     assert _rel(got, ref) < 3e-2
 
 
-def test_cached_decode_matches_longer_prefill(cuda):
+@pytest.mark.parametrize("fmt", ["int4", "fp4_e2m1"])
+def test_cached_decode_matches_longer_prefill(cuda, fmt):
     from apsi_b200.decoder import QuantDecoder, DecoderConfig
     from apsi_b200 import kernels
-    model = QuantDecoder(DecoderConfig(**SMALL), device=cuda, fmt="int4", seed=4)
+    model = QuantDecoder(DecoderConfig(**SMALL), device=cuda, fmt=fmt, seed=4)
     ids = torch.randint(0, SMALL["V"], (2, 21), device=cuda, generator=torch.Generator(device=cuda).manual_seed(2))
     cache = model.new_cache(2, 32)
     model.prefill(ids[:, :20], cache)
