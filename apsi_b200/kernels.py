@@ -175,6 +175,7 @@ def dequant(fmt, codes, scales, N, K, out_dtype=torch.float32, scale_f32=None):
 # ------------------------------------------------------------------------------------------------ products
 _ws_lock = threading.Lock()
 _ws = {}
+_ws_retired = []   # outgrown workspaces stay allocated: a captured CUDA graph may still use their addresses
 
 
 def linear_workspace_bytes(fmt, M, N, K):
@@ -184,14 +185,19 @@ def linear_workspace_bytes(fmt, M, N, K):
 
 
 def _workspace(device, nbytes):
-    """A per-device scratch buffer of at least nbytes (grown on demand, never shrunk)."""
+    """A per-device scratch buffer of at least nbytes (grown on demand, never shrunk).  A buffer that is
+    outgrown is kept, not freed: a CUDA graph captured with it replays into its address, so that memory must
+    not pass to another tensor.  The cost is at most the sum of the sizes on the way to the largest."""
     if nbytes == 0:
         return None
     key = device.index if device.index is not None else torch.cuda.current_device()
     with _ws_lock:
         buf = _ws.get(key)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            if buf is not None:
+                _ws_retired.append(buf)
+            buf = torch.zeros(max(nbytes, 2 * (buf.numel() if buf is not None else 0), 1 << 20), dtype=torch.uint8,
+                              device=device)
             _ws[key] = buf
         return buf
 
