@@ -20,9 +20,9 @@
 //   warps 2..9    dequantise one row x one half of the stage's K into the A tile (st.shared + proxy fence)
 //   warps 10..13  epilogue: tcgen05.ld -> scale / bias / accumulate -> bf16 -> global
 // All mbarrier waits are bounded (lb::mbar_wait); a timeout sets the device error word and the CTA drains.
-#include <cuda.h>
 #include <string.h>
 #include "lb_common.cuh"
+#include "lb_tmap.h"
 #include "lb_kernels.h"
 
 namespace lb {
@@ -466,22 +466,6 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------- host side
-typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static PFN_encodeTiled get_encode() {
-  static PFN_encodeTiled fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_encodeTiled>(ptr);
-  }
-  return fn;
-}
-
 static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
 
 size_t gemm_smem_bytes(int fmt, int bn) {

@@ -33,8 +33,16 @@
 //
 // With programmatic dependent launch (static weights), the producer streams weights before the previous
 // kernel on the stream has finished; only the activations and the output wait for it (griddepcontrol.wait).
+//
+// Box mode (template flag BOX): instead of one bulk copy per row, the producer fetches a whole item with ONE tensor copy of a
+// 3-D box (64 bytes of a unit x 16 rows x 32 units) over the codes in their stored [N, K/2] layout, which lands
+// in shared memory unit-major ([unit][row][64 B]: conflict-free 16-byte reads, no padding), plus, when the
+// scale rows are 16-byte multiples (K % 1024 == 0), the item's 16 x 32 fp16 scales as a 2-D box.  Rows past N
+// and units past the row are zero-filled by the copy and never read.  The arithmetic and its order are the same
+// in both modes, so both give the same bits.
 #include "lb_common.cuh"
 #include "lb_kernels.h"
+#include "lb_tmap.h"
 
 namespace lb {
 
@@ -51,6 +59,9 @@ constexpr int MAX_CLUSTER = 8;
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int HALF_SM_SMEM = 113 * 1024;        // two CTAs per SM
 constexpr int MAX_SLOTS = 8;
+constexpr int BOX_CODES = RB * RANGE_UNITS * UNIT;   // 32768: box mode, [unit][row][64 B]
+constexpr int BOX_SCALES = RB * RANGE_UNITS * 2;     // 1024: box mode, fp16 [row][unit]
+static_assert(BOX_CODES + BOX_SCALES <= STAGE_BYTES, "box mode item must fit a ring slot");
 }  // namespace gemv
 
 struct GemvParams {
@@ -72,6 +83,7 @@ struct GemvParams {
   const void* ln;         // RMSNorm weights [K] (float32 or bf16) of the norm prologue, or null
   int ln_f32, ln_vec;     // weights are float32; weights are 16-byte aligned
   float ln_eps, ln_off;
+  int scale_tma;          // box mode: the item's scales come with it (tensor map `ts`)
 };
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
@@ -250,6 +262,36 @@ __device__ __forceinline__ void unit_i8(const uint4& w0, const uint4& w8, const 
   }
 }
 
+// The same unit with fewer instructions: the codes of the even positions become bytes q + 8 and those of the
+// odd positions bytes 16 (q + 8), each with ONE LOP3 and no shift, so the MMAs are regrouped by position
+// class -- ae takes the even positions of two words at a time, ao the odd ones (scaled by 16) -- against the
+// same staged B fragments.  ae + ao / 16 is the exact integer unit_i8 forms, and v = 256 hi + lo is formed from
+// 16 v (exact, |16 v| < 2^31) with one arithmetic shift, so `acc` gets the same bits.  `sf` is s * 2^e of the
+// unit (0 for a unit past the row: its finite garbage then adds exactly nothing).
+__device__ __forceinline__ void unit_i8_lean(const uint4& w0, const uint4& w8, const uint4& b0, const uint4& b1,
+                                             int nc0, int nc1, float sf0, float sf8, float& acc0, float& acc8) {
+  const uint32_t W0[4] = {w0.x ^ 0x88888888u, w0.y ^ 0x88888888u, w0.z ^ 0x88888888u, w0.w ^ 0x88888888u};
+  const uint32_t W8[4] = {w8.x ^ 0x88888888u, w8.y ^ 0x88888888u, w8.z ^ 0x88888888u, w8.w ^ 0x88888888u};
+  int ae[4] = {-nc0, -nc1, -nc0, -nc1};
+  int ao[4] = {0, 0, 0, 0};
+  {
+    const uint32_t e[4] = {W0[0] & 0x0F0F0F0Fu, W8[0] & 0x0F0F0F0Fu, W0[1] & 0x0F0F0F0Fu, W8[1] & 0x0F0F0F0Fu};
+    const uint32_t o[4] = {W0[0] & 0xF0F0F0F0u, W8[0] & 0xF0F0F0F0u, W0[1] & 0xF0F0F0F0u, W8[1] & 0xF0F0F0F0u};
+    mma_u8s8(ae, e, b0.x, b0.z);
+    mma_u8s8(ao, o, b0.y, b0.w);
+  }
+  {
+    const uint32_t e[4] = {W0[2] & 0x0F0F0F0Fu, W8[2] & 0x0F0F0F0Fu, W0[3] & 0x0F0F0F0Fu, W8[3] & 0x0F0F0F0Fu};
+    const uint32_t o[4] = {W0[2] & 0xF0F0F0F0u, W8[2] & 0xF0F0F0F0u, W0[3] & 0xF0F0F0F0u, W8[3] & 0xF0F0F0F0u};
+    mma_u8s8(ae, e, b1.x, b1.z);
+    mma_u8s8(ao, o, b1.y, b1.w);
+  }
+  const int v0 = ((ae[0] * 16 + ao[0]) * 256 + (ae[1] * 16 + ao[1])) >> 4;
+  const int v8 = ((ae[2] * 16 + ao[2]) * 256 + (ae[3] * 16 + ao[3])) >> 4;
+  acc0 = fmaf(static_cast<float>(v0), sf0, acc0);
+  acc8 = fmaf(static_cast<float>(v8), sf8, acc8);
+}
+
 // Shared-memory carve-up, in bytes from the base of dynamic shared memory.
 struct GemvSmem {
   int ring, xs, corr, xsc, gred, ptab, zeros, bars, lnf, total;
@@ -266,7 +308,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int fmt, int M, int MT, int G, int
   s.xs = slots * STAGE_BYTES;                                  // multiple of 128
   s.corr = s.xs + ((M * s.token_stride + 127) & ~127);
   s.xsc = s.corr + ((M * xs_units * (fmt == 20 ? 12 : 4) + 127) & ~127);   // int core: int2 + 2^e; else float
-  s.gred = s.xsc + 2 * 16 * MAX_RANGES * 4;                    // xsc + xmax
+  s.gred = s.xsc + (fmt == 20 ? 0 : 2 * 16 * MAX_RANGES * 4);  // xsc + xmax (unused on the integer path)
   s.ptab = s.gred + G * 2 * GW * 32 * (fmt == 20 ? 2 : 4) * MT * 4;   // double-buffered group partials
   s.zeros = s.ptab + ((items * 16 * M * 4 + 127) & ~127);
   s.bars = s.zeros + 256;                                      // 256 zero bytes (absent tokens)
@@ -306,8 +348,9 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int64_t n, int to
   *yp = f32_to_bf16_bits(v);
 }
 
-template <int FMT, int MT, int G, int MINB>
-__global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(const GemvParams p) {
+template <int FMT, int MT, int G, int MINB, bool BOX, bool LR = false>
+__global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
+    gemv_kernel(const GemvParams p, const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts) {
   using namespace gemv;
   constexpr int NCW = G * GW;                  // consumer warps
   constexpr int CT = NCW * 32;                 // consumer threads
@@ -355,7 +398,8 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     *abort_v = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < 16 * MAX_RANGES; i += blockDim.x) xmax[i] = 0;
+  if (FMT != 20)
+    for (int i = threadIdx.x; i < 16 * MAX_RANGES; i += blockDim.x) xmax[i] = 0;
   for (int i = threadIdx.x; i < 64; i += blockDim.x) reinterpret_cast<uint32_t*>(dyn_smem + L.zeros)[i] = 0u;
   __syncthreads();
   pdl_launch_dependents();
@@ -365,6 +409,10 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
     // lane 0 registers the byte count, lanes 0..15 copy one row each; the weights do not depend on earlier
     // kernels, so streaming starts before griddepcontrol.wait
     const uint64_t wpol = l2_policy_evict_first();   // the weights are read once
+    if (BOX && lane == 0) {
+      prefetch_tmap(&tw);
+      if (p.scale_tma) prefetch_tmap(&ts);
+    }
     for (int q = 0; q < nq && !*abort_v; ++q) {
       const int k = q / nloc, i = q - k * nloc;
       const int64_t row0 = static_cast<int64_t>(cid + k * p.C) * RB;
@@ -373,6 +421,16 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       const uint32_t bytes_row = static_cast<uint32_t>(min(p.total_units - u0, RANGE_UNITS) * UNIT);
       const int slot = ring_slot(q, slots);
       if (q >= slots) mbar_wait(&empty_bar[slot], ((q / slots) - 1) & 1, abort_v);
+      if (BOX) {                            // one box per item: codes [unit][row][64 B] (+ scales [row][unit])
+        if (lane == 0) {
+          uint8_t* dst = ring + slot * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[slot], BOX_CODES + (p.scale_tma ? BOX_SCALES : 0));
+          tma_load_3d_hint(dst, &tw, 0, static_cast<int>(row0), u0, &full_bar[slot], wpol);
+          if (p.scale_tma) tma_load_2d(dst + BOX_CODES, &ts, u0, static_cast<int>(row0), &full_bar[slot]);
+        }
+        __syncwarp();
+        continue;
+      }
       if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], bytes_row * rows_valid);
       __syncwarp();
       if (lane < rows_valid)
@@ -672,13 +730,15 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       const int uend = min(u0 + RANGE_UNITS, p.total_units);
       const int64_t rg = row0 + g < p.N ? row0 + g : p.N - 1;
       const int64_t rg8 = row0 + g + 8 < p.N ? row0 + g + 8 : p.N - 1;
-      // scales first (their latency overlaps the wait for the codes)
+      // scales first (their latency overlaps the wait for the codes); in box mode with scale boxes they
+      // arrive with the codes
+      const bool sc_in_slot = BOX && p.scale_tma;
       float sc[UPW][2];
 #pragma unroll
       for (int h = 0; h < UPW; ++h) {
         sc[h][0] = sc[h][1] = 1.f;
         const int uu = u0 + gw + h * GW;
-        if (I4 && uu < uend) {
+        if (I4 && uu < uend && !sc_in_slot) {
           sc[h][0] = __half2float(__ldg(p.s16 + rg * ng + uu));
           sc[h][1] = __half2float(__ldg(p.s16 + rg8 * ng + uu));
         }
@@ -686,8 +746,43 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
       const int slot = ring_slot(q, slots);
       mbar_wait(&full_bar[slot], (q / slots) & 1, abort_v);
       const uint32_t sbuf = ring_base + slot * STAGE_BYTES;
-      // all of this warp's codes of the item go to registers, then the slot is released at once
-      uint4 wr[UPW][2];
+      // all of this warp's codes of the item go to registers, then the slot is released at once (LR: the codes
+      // are read from the slot unit by unit and the slot is released after the multiply)
+      constexpr bool HOLD = BOX && LR && FMT == 20;
+      uint4 wr[HOLD ? 1 : UPW][2];
+      const uint32_t code_base = sbuf + g * UNIT;          // box mode: unit j's row g at j * 1024 + g * 64
+      if constexpr (HOLD) {
+        const uint32_t sscale = smem_u32(ring) + slot * STAGE_BYTES + BOX_CODES;
+#pragma unroll
+        for (int h = 0; h < UPW; ++h) {
+          const int j = gw + h * GW;
+          if (sc_in_slot && u0 + j < uend) {
+            __half_raw h0, h8;
+            h0.x = static_cast<unsigned short>(lds_u16(sscale + (g * RANGE_UNITS + j) * 2));
+            h8.x = static_cast<unsigned short>(lds_u16(sscale + ((g + 8) * RANGE_UNITS + j) * 2));
+            sc[h][0] = __half2float(__half(h0));
+            sc[h][1] = __half2float(__half(h8));
+          }
+        }
+      } else if constexpr (BOX) {
+        // [unit][row][64 B]: unit j's row g at j * 1024 + g * 64 (ring_base already adds c * 16)
+        const uint32_t sb = sbuf;
+        const uint32_t sscale = smem_u32(ring) + slot * STAGE_BYTES + BOX_CODES;
+#pragma unroll
+        for (int h = 0; h < UPW; ++h) {
+          const int j = gw + h * GW;
+          const uint32_t a = sb + j * (RB * UNIT) + g * UNIT;
+          wr[h][0] = lds_v4(a);
+          wr[h][1] = lds_v4(a + 8 * UNIT);
+          if (I4 && sc_in_slot && u0 + j < uend) {
+            __half_raw h0, h8;
+            h0.x = static_cast<unsigned short>(lds_u16(sscale + (g * RANGE_UNITS + j) * 2));
+            h8.x = static_cast<unsigned short>(lds_u16(sscale + ((g + 8) * RANGE_UNITS + j) * 2));
+            sc[h][0] = __half2float(__half(h0));
+            sc[h][1] = __half2float(__half(h8));
+          }
+        }
+      } else {
 #pragma unroll
       for (int h = 0; h < UPW; ++h) {
         const int uu = u0 + gw + h * GW;
@@ -700,50 +795,49 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB) gemv_kernel(con
           wr[h][1] = wr[h][0];
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[slot]);
+      }
+      if (!HOLD) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[slot]);
+      }
       float acc[MT][PW];
 #pragma unroll
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int j = 0; j < PW; ++j) acc[t][j] = 0.f;
       if constexpr (FMT == 20) {
+        // one 4-token tile (M <= 2 here: columns 2 tok, 2 tok + 1 are the hi / lo digits of token tok = c)
         const int* corr_i = reinterpret_cast<const int*>(corr);
         const float* fac = corr + 2 * p.M * units_staged;
-        float accT[MT][2];
-#pragma unroll
-        for (int T = 0; T < MT; ++T) accT[T][0] = accT[T][1] = 0.f;
+        const int ncols = 2 * p.M;
+        const int tok = c < p.M ? c : 0;                  // lanes of absent tokens compute unused columns
+        const int uloc0 = il * RANGE_UNITS + gw;          // unit h of this warp: uloc0 + h * GW
+        const uint8_t* xb = xs + uloc0 * (ncols * 128) + (g < ncols ? g : 0) * 64 + c * 16;
+        const int ci = tok * units_staged + uloc0;
+        float a0 = 0.f, a8 = 0.f;
 #pragma unroll
         for (int h = 0; h < UPW; ++h) {
-          const int uu = u0 + gw + h * GW;
-          if (uu >= uend) continue;
-          const int uloc = il * RANGE_UNITS + (uu - u0);
-          uint32_t Bq[MT][8];
-          int nc[MT][2];
-          float fT[MT];
-#pragma unroll
-          for (int T = 0; T < MT; ++T) {
-            const int ncols = min(8, 2 * p.M - 8 * T);
-            const uint32_t a = smem_u32(xs) + T * units_staged * 1024 + uloc * (ncols * 128) + g * 64 + c * 16;
-            const bool colok = g < ncols;
-            const uint4 b0 = lds_v4(colok ? a : zbase);
-            const uint4 b1 = lds_v4(colok ? a + ncols * 64 : zbase + 16);
-            Bq[T][0] = b0.x; Bq[T][1] = b0.y; Bq[T][2] = b0.z; Bq[T][3] = b0.w;
-            Bq[T][4] = b1.x; Bq[T][5] = b1.y; Bq[T][6] = b1.z; Bq[T][7] = b1.w;
-            const int tok = 4 * T + c;
-            if (tok < p.M) {
-              const int2 cv = *reinterpret_cast<const int2*>(corr_i + (tok * units_staged + uloc) * 2);
-              nc[T][0] = cv.x; nc[T][1] = cv.y;
-              fT[T] = fac[tok * units_staged + uloc];
-            } else {
-              nc[T][0] = nc[T][1] = 0;
-              fT[T] = 0.f;
-            }
+          const bool ok = u0 + gw + h * GW < uend;
+          const uint8_t* bp = xb + h * GW * (ncols * 128);
+          const uint4 b0 = *reinterpret_cast<const uint4*>(bp);
+          const uint4 b1 = *reinterpret_cast<const uint4*>(bp + ncols * 64);
+          const int2 cv = *reinterpret_cast<const int2*>(corr_i + (ci + h * GW) * 2);
+          const float f = fac[ci + h * GW];
+          const float sf0 = ok ? sc[h][0] * f : 0.f;
+          const float sf8 = ok ? sc[h][1] * f : 0.f;
+          if constexpr (HOLD) {
+            const uint32_t a = code_base + (gw + h * GW) * (RB * UNIT);
+            unit_i8_lean(lds_v4(a), lds_v4(a + 8 * UNIT), b0, b1, cv.x, cv.y, sf0, sf8, a0, a8);
+          } else {
+            unit_i8_lean(wr[h][0], wr[h][1], b0, b1, cv.x, cv.y, sf0, sf8, a0, a8);
           }
-          unit_i8<MT>(wr[h][0], wr[h][1], Bq, nc, fT, sc[h][0], sc[h][1], accT);
         }
-#pragma unroll
-        for (int T = 0; T < MT; ++T) { acc[T][0] = accT[T][0]; acc[T][1] = accT[T][1]; }
+        if constexpr (HOLD) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty_bar[slot]);
+        }
+        acc[0][0] = a0;
+        acc[0][1] = a8;
       } else {
 #pragma unroll
       for (int h = 0; h < UPW; ++h) {
@@ -940,10 +1034,11 @@ int gemv_max_k(int fmt) {
   return gemv::MAX_RANGES * gemv::RANGE_UNITS * gemv::UNIT * ((fmt == 2 || fmt == 9) ? 2 : 1);
 }
 
-template <int FMT, int MT, int G, int MINB>
-static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max_slots, bool pdl, cudaStream_t st) {
+template <int FMT, int MT, int G, int MINB, bool BOX = false, bool LR = false>
+static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max_slots, bool pdl, cudaStream_t st,
+                                 const CUtensorMap* tw = nullptr, const CUtensorMap* ts = nullptr) {
   using namespace gemv;
-  auto kern = gemv_kernel<FMT, MT, G, MINB>;
+  auto kern = gemv_kernel<FMT, MT, G, MINB, BOX, LR>;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -964,7 +1059,9 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
   int R = 1;
   const int rmax = p.nr < MAX_CLUSTER ? p.nr : MAX_CLUSTER;
   auto clusters_for = [&](int R_) { int c = target / R_; return c < p.nblocks ? c : p.nblocks; };
-  while (R < rmax && (smem_for(R, G, clusters_for(R)) > limit || clusters_for(R) * R < target / 2)) ++R;
+  // box mode keeps at least two items in flight per CTA (its slots are the only ring a group has)
+  const int fit_slots = BOX ? (2 * G <= max_slots ? 2 * G : G) : G;
+  while (R < rmax && (smem_for(R, fit_slots, clusters_for(R)) > limit || clusters_for(R) * R < target / 2)) ++R;
   if (smem_for(R, G, clusters_for(R)) > limit && limit < SMEM_LIMIT) {   // one CTA per SM after all
     limit = SMEM_LIMIT;
     target = sms;
@@ -1002,7 +1099,41 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
   cfg.blockDim = dim3((G * GW + 1) * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  return cudaLaunchKernelEx(&cfg, kern, p);
+  static const CUtensorMap none = {};
+  return cudaLaunchKernelEx(&cfg, kern, p, tw ? *tw : none, ts ? *ts : none);
+}
+
+// Tensor maps of box mode: codes as a 3-D tensor (64 bytes of a unit, row, unit) whose box lands [unit][row][64 B]
+// in shared memory; scales as a 2-D tensor (unit, row) when a scale row is a multiple of 16 bytes.
+static bool encode_gemv_boxes(const void* codes, const void* scales, int64_t N, int64_t K, bool i4, CUtensorMap* tw,
+                              CUtensorMap* ts, bool* scale_tma) {
+  using namespace gemv;
+  PFN_encodeTiled enc = get_encode();
+  if (!enc || N > (1LL << 31)) return false;
+  const int64_t row_bytes = i4 ? K / 2 : K;
+  const int64_t units = row_bytes / UNIT;
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(UNIT), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(units)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(UNIT)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(UNIT), static_cast<cuuint32_t>(RB), static_cast<cuuint32_t>(RANGE_UNITS)};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(codes), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  *scale_tma = false;
+  if (i4 && (units * 2) % 16 == 0) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(units), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(units * 2)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(RANGE_UNITS), static_cast<cuuint32_t>(RB)};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(scales), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      *scale_tma = true;
+  }
+  return true;
 }
 
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
@@ -1028,6 +1159,7 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.ln_vec = (ln && (reinterpret_cast<uintptr_t>(ln->w) & 15) == 0) ? 1 : 0;
   p.ln_eps = ln ? ln->eps : 0.f;
   p.ln_off = ln ? ln->off : 0.f;
+  p.scale_tma = 0;
   if (fmt == 7 || fmt == 8) {
     if (ln) return cudaErrorNotSupported;     // the norm prologue lives in gemv_kernel's staging
     const int64_t want = (N + 7) / 8;         // one warp per row
@@ -1048,6 +1180,18 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   // [11008, 4096] at M = 2: 9.38 -> 8.78 us); more tokens on the bf16 path, whose n8 tile holds eight tokens
   // (the integer path measured 5 % slower at M = 4 and 25-60 % slower at M = 8: heavier staging, two tiles)
   if (fmt == 2) {
+#ifndef LB_GEMV_NO_BOX
+    if (M <= 2) {
+      // box mode: one tensor copy per item (codes, and scales when their rows allow it); three groups, one slot
+      // each ([28672, 8192]: 31.7 -> 29.2 us, [8192, 28672]: 40.3 -> 36.7 us against one copy per row)
+      CUtensorMap tw, ts;
+      bool stma = false;
+      if (encode_gemv_boxes(codes, scales, N, K, true, &tw, &ts, &stma)) {
+        p.scale_tma = stma ? 1 : 0;
+        return launch_gemv_t<20, 1, 3, 1, true>(p, sms, 1, 3, pdl, st, &tw, &ts);
+      }
+    }
+#endif
     if (M <= 2) return launch_gemv_t<20, 1, 3, 1>(p, sms, 1, 6, pdl, st);
     // several K ranges per row (K > 4096) and more than four tokens: the ring holds four slots with two groups
     // against three with three groups once the larger activation staging is placed (measured on [4096, 11008]

@@ -14,8 +14,13 @@
 //   * there is ONE scratch per device: two calls whose prefill kernels overlap in time on one device (two
 //     streams, or two host threads) race on it and corrupt each other's outputs.  Calls in order on one
 //     stream are safe;
-//   * the first call on a device looks the array's address up (cudaGetSymbolAddress); make that first call
-//     outside any stream capture.
+//   * host code cannot use the array's name as a device address: the address is looked up with
+//     cudaGetSymbolAddress on the first call in each CUDA context of a device (the primary context, a context
+//     made current through the driver API, or a new primary context after cudaDeviceReset: the cache is keyed
+//     by the context's unique id) and reused after that; make that first call outside any stream capture.
+#include <cuda.h>
+#include <mutex>
+
 #include "../../include/apsi_lowbit.h"
 #include "lb_common.cuh"
 #include "lb_kernels.h"
@@ -25,21 +30,55 @@ namespace lb {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LB_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-void* g_scratch_ptr[64];          // per device; set once
+struct ScratchSlot {
+  unsigned long long ctx_id = 0;  // unique id of the context the address belongs to (0: none yet)
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[64];        // per device
 std::mutex g_scratch_mu;
+
+typedef CUresult (*PFN_ctxGetCurrent)(CUcontext*);
+typedef CUresult (*PFN_ctxGetId)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context (0 when it cannot be read).
+unsigned long long current_ctx_id() {
+  static PFN_ctxGetCurrent get_cur = nullptr;
+  static PFN_ctxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &q1) == cudaSuccess &&
+        q1 == cudaDriverEntryPointSuccess &&
+        cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &q2) == cudaSuccess &&
+        q2 == cudaDriverEntryPointSuccess) {
+      get_cur = reinterpret_cast<PFN_ctxGetCurrent>(a);
+      get_id = reinterpret_cast<PFN_ctxGetId>(b);
+    }
+  });
+  if (!get_cur || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_cur(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 int scratch_for_device(int dev, void** out) {
   if (dev < 0 || dev >= 64) return fail(LB_E_DEVICE, "device %d out of range", dev);
+  const unsigned long long id = current_ctx_id();
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  ScratchSlot& s = g_scratch[dev];
+  if (!s.ptr || id == 0 || s.ctx_id != id) {   // unknown context id: look the address up every time
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // the current device's copy
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // this context's copy of the array
     if (e != cudaSuccess || !p)
       return fail(LB_E_DEVICE, "lb_linear_noalloc: cudaGetSymbolAddress of the scratch failed on device %d: %s",
                   dev, cudaGetErrorString(e));
-    g_scratch_ptr[dev] = p;
+    s.ptr = p;
+    s.ctx_id = id;
   }
-  *out = g_scratch_ptr[dev];
+  *out = s.ptr;
   return LB_OK;
 }
 }  // namespace

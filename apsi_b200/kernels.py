@@ -187,7 +187,11 @@ def linear_workspace_bytes(fmt, M, N, K):
 def _workspace(device, nbytes):
     """A per-device scratch buffer of at least nbytes (grown on demand, never shrunk).  A buffer that is
     outgrown is kept, not freed: a CUDA graph captured with it replays into its address, so that memory must
-    not pass to another tensor.  The cost is at most the sum of the sizes on the way to the largest."""
+    not pass to another tensor.  The cost is at most the sum of the sizes on the way to the largest.
+
+    There is ONE buffer per device, shared by every stream: two prefill products (M > 16) issued on different
+    streams of one device at the same time race on it.  Serialise prefill calls per device (one stream, or
+    events between the streams)."""
     if nbytes == 0:
         return None
     key = device.index if device.index is not None else torch.cuda.current_device()
@@ -212,6 +216,48 @@ def _fn(name):
     return f
 
 
+def _code_bytes(fmt, N, K):
+    """(bytes of the codes, bytes of the scales) lb_linear reads for a [N, K] weight in format ``fmt``."""
+    if fmt == FMT_INT4_G128:
+        return N * K // 2, N * (K // 128) * 2
+    if fmt == FMT_INT8_ROW:
+        return N * K, N * 2
+    if fmt in (_lib.FMT_FP8_E4M3, _lib.FMT_FP8_E5M2):
+        return N * K, N * 4
+    if fmt == _lib.FMT_FP4_E2M1:
+        return N * K // 2, N * 4
+    if fmt in (_lib.FMT_FP6_E3M2, _lib.FMT_FP6_E2M3):
+        return N * K * 3 // 4, N * 4
+    return 0, 0
+
+
+def _check_product(fmt, x, M, K, codes, scales, N, bias, out):
+    """The operand checks of a product, so that nothing the library is given lies outside its tensor: codes,
+    scales and bias hold what the format needs for [N, K] on x's device, and out is a bfloat16 [>= M, >= N] view
+    with unit column stride on that device.  Raises LowbitError(LB_E_ARG)."""
+    dev = x.device
+    cb, sb = _code_bytes(fmt, N, K)
+    for t, name, need in ((codes, "codes", cb), (scales, "scales", sb)):
+        if not isinstance(t, torch.Tensor) or t.device != dev:
+            raise LowbitError(_lib.LB_E_ARG, f"{name} must be a CUDA tensor on {dev}")
+        if t.numel() * t.element_size() < need:
+            raise LowbitError(_lib.LB_E_ARG, f"{name} holds {t.numel() * t.element_size()} bytes, the format needs "
+                                             f"{need} for N={N}, K={K}")
+        if not t.is_contiguous():
+            raise LowbitError(_lib.LB_E_ARG, f"{name} must be contiguous")
+    if bias is not None:
+        if (not isinstance(bias, torch.Tensor) or bias.device != dev or bias.dtype != torch.bfloat16
+                or bias.numel() < N or not bias.is_contiguous()):
+            raise LowbitError(_lib.LB_E_ARG, f"bias must be a contiguous bfloat16 tensor of {N} values on {dev}")
+    if out.dtype != torch.bfloat16 or out.device != dev:
+        raise LowbitError(_lib.LB_E_ARG, f"out must be a bfloat16 tensor on {dev}")
+    if out.dim() == 0 or out.stride(-1) != 1 or out.shape[-1] < N:
+        raise LowbitError(_lib.LB_E_ARG, f"out must have unit column stride and at least N={N} columns")
+    rows = out.numel() // max(out.shape[-1], 1)
+    if rows < M or (out.dim() > 2 and not out.is_contiguous()):
+        raise LowbitError(_lib.LB_E_ARG, f"out must hold M={M} rows of a row-major [M, ldy] output")
+
+
 def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False, static_weights=False):
     """y[M, N] = x[M, K] . deq(W)^T (+ bias) (+ out if accumulate), bf16 out, fp32 accumulation.
 
@@ -231,6 +277,7 @@ def linear(fmt, x, codes, scales, N, bias=None, out=None, accumulate=False, stat
         if accumulate:
             raise LowbitError(_lib.LB_E_ARG, "accumulate needs an output tensor")
         out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    _check_product(fmt, x, M, K, codes, scales, N, bias, out)
     ldy = out.stride(-2) if out.dim() >= 2 else N
     switch = dev.index != torch.cuda.current_device()
     if switch:
@@ -418,6 +465,7 @@ def linear_rms(fmt, x, ln, codes, scales, N, eps=1e-6, off=0.0, bias=None, out=N
         if accumulate:
             raise LowbitError(_lib.LB_E_ARG, "accumulate needs an output tensor")
         out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    _check_product(fmt, x, M, K, codes, scales, N, bias, out)
     ldy = out.stride(-2) if out.dim() >= 2 else N
     wdt = _lib.DT_F32 if ln.dtype == torch.float32 else _lib.DT_BF16
     with torch.cuda.device(dev):

@@ -11,8 +11,9 @@ Same names and argument meanings as the reference module (apsi/lowbit.py:15-181)
   same bits as the reference, signed zeros included.  int8 and int4 are on the B200 path; the minifloat kinds (fp8, fp6,
   fp4) raise ``LowbitError``.
 * ``matmul(x, w)`` -- the dispatch point.  A packed weight (``precision.QTensor`` from ``quantize_linear``)
-  runs the fused dequantise-and-matmul kernels.  A dense weight keeps the reference behaviour: ``x @ w``, or
-  fp8 tensor cores through ``torch._scaled_mm`` when ``_HW["on"]``.  ``fp8_matmul_available`` is unchanged.
+  runs the fused dequantise-and-matmul kernels.  A dense weight gives ``x @ w``, or, when ``_HW["on"]``, an fp8
+  product on the library's fp8 kernels (w rounded to e4m3 per output column; backward in bfloat16).
+  ``fp8_matmul_available`` answers the reference's question for this library.
 
 Every rounding runs on the GPU: NumPy arrays are copied to the current CUDA device and back.  Without a GPU or
 the library these calls raise; there is no CPU fallback.
@@ -133,52 +134,78 @@ def round_tree(params, kind):
 
 
 # ---------------------------------------------------------------------- products
+# The dense-weight switch of the reference (apsi/lowbit.py:116): off unless a caller turns it on.  "why" stays
+# for callers that read it; nothing here writes it (a failing fp8 product raises instead of switching off).
 _HW = {"on": False, "why": None}
 
 
 def fp8_matmul_available(dev):
-    """True when this GPU and PyTorch can multiply in fp8 on tensor cores (compute capability 8.9 and up)."""
+    """Whether ``matmul`` can take dense weights through fp8 on this device (the reference's query,
+    apsi/lowbit.py:119-131): a CUDA device of compute capability 10.x with this library loaded, unless the
+    environment variable APSI_FP8_MATMUL is 0, false or no."""
     import os
     import torch
     if os.environ.get("APSI_FP8_MATMUL", "1").strip().lower() in ("0", "false", "no"):
         return False
-    if dev.type != "cuda" or not hasattr(torch, "_scaled_mm") or not hasattr(torch, "float8_e4m3fn"):
+    if getattr(dev, "type", None) != "cuda" or not torch.cuda.is_available():
         return False
+    if torch.cuda.get_device_capability(dev)[0] != 10:
+        return False
+    from . import _lib
     try:
-        return tuple(torch.cuda.get_device_capability(dev)) >= (8, 9)
-    except Exception:                                   # noqa: BLE001
+        _lib.load()
+    except LowbitError:
         return False
+    return True
 
 
-def _fp8_product(x2, w):
-    """x2 @ w with both in fp8 E4M3 (one scale each) on the tensor cores, bfloat16 out (dense weights only)."""
+_FP8 = {}
+
+
+def _fp8_dense():
+    """The autograd function of the dense fp8 product (built once, when torch is first needed).
+
+    Forward: w [K, N] is rounded to fp8 e4m3 per output column (one float32 scale per column: the library's
+    per-row minifloat quantiser on w^T) and multiplied with x in bfloat16 by the library's fused fp8 product
+    (the codes become exact fp16 operands; float32 accumulation; bfloat16 out).  The reference instead rounds x
+    and w to e4m3 with one scale each and calls cuBLASLt (apsi/lowbit.py:133-160); rounding only w, per column,
+    keeps x exact and loses less.  Backward: in bfloat16 on the unrounded operands, as the reference's does:
+    dx = g w^T, dw = x^T g."""
+    if "fn" in _FP8:
+        return _FP8["fn"]
     import torch
-    xs = (x2.detach().abs().amax().float() / 448.0).clamp(min=1e-12)
-    ws = (w.detach().abs().amax().float() / 448.0).clamp(min=1e-12)
-    a = (x2.float() / xs).to(torch.float8_e4m3fn)
-    b = (w.float() / ws).to(torch.float8_e4m3fn).t().contiguous().t()
-    y = torch._scaled_mm(a, b, scale_a=xs, scale_b=ws, out_dtype=torch.bfloat16)
-    return y[0] if isinstance(y, tuple) else y
+    from ._lib import FMT_FP8_E4M3
+
+    class Fp8Dense(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, x2, w):
+            N = w.shape[1]
+            codes, s32 = _k.quant_minifloat(w.detach().t().float().contiguous(), FMT_FP8_E4M3, per_row=True)
+            y = _k.linear(FMT_FP8_E4M3, x2.detach().to(torch.bfloat16).contiguous(), codes, s32, N)
+            ctx.save_for_backward(x2, w)
+            return y
+
+        @staticmethod
+        def backward(ctx, g):
+            x2, w = ctx.saved_tensors
+            gb = g.to(torch.bfloat16)
+            gx = gb @ w.to(torch.bfloat16).t()
+            gw = x2.to(torch.bfloat16).t() @ gb
+            return gx.to(x2.dtype), gw.to(w.dtype)
+
+    _FP8["fn"] = Fp8Dense
+    return Fp8Dense
 
 
 def matmul(x, w):
-    """x @ w.  A packed weight (precision.QTensor) runs the fused dequantise-and-matmul kernels; a dense one
-    the ordinary product, or fp8 tensor cores when that is switched on and the shapes allow it."""
+    """x @ w.  A packed weight (precision.QTensor) runs the fused dequantise-and-matmul kernels.  A dense weight
+    gives the ordinary product, or, when ``_HW["on"]`` and K is a multiple of 64, the fp8 product of
+    ``_fp8_dense`` (bfloat16 out, with a gradient).  Errors of the fp8 path are raised, not hidden."""
     from . import precision
     if isinstance(w, precision.QTensor):
         return precision.qmatmul(x, w)
-    if not _HW["on"] or not x.is_cuda or w.dim() != 2 or x.shape[-1] % 16 or w.shape[1] % 16:
+    if not _HW["on"] or not x.is_cuda or w.dim() != 2 or x.shape[-1] % 64:
         return x @ w
-    import torch
     K = x.shape[-1]
-    x2 = x.reshape(-1, K)
-    M = x2.shape[0]
-    pad = (-M) % 16
-    if pad:
-        x2 = torch.cat([x2, x2.new_zeros((pad, K))])
-    try:
-        y = _fp8_product(x2.contiguous(), w)
-    except Exception as e:                              # noqa: BLE001 - never fail a run over the fp8 path
-        _HW["on"], _HW["why"] = False, f"{type(e).__name__}: {e}"
-        return x @ w
-    return y[:M].reshape(*x.shape[:-1], w.shape[1])
+    y = _fp8_dense().apply(x.reshape(-1, K).contiguous(), w)
+    return y.reshape(*x.shape[:-1], w.shape[1])

@@ -26,7 +26,7 @@ No GPU is needed to save or load; ``load_packed(..., device=...)`` also places t
 import hashlib
 import json
 import os
-import struct
+import tempfile
 
 import numpy as np
 
@@ -115,74 +115,139 @@ def _entries(params):
     return tensors, qts
 
 
-def save_packed(path, params, metadata=None):
-    """Write a parameter tree (dicts / lists of arrays and packed QTensors) as one ``.apsim`` file."""
-    path = str(path)
-    if not path.endswith(".apsim"):
-        path += ".apsim"
-    tensors, qts = _entries(params)
-    header, offset = {}, 0
+_MAX_HEADER = 256 << 20      # a header above this is treated as damage, not read into memory
+_CHUNK = 16 << 20            # bytes hashed per read
+
+
+def _table(tensors):
+    """Tensor table of the container: each tensor's dtype tag, shape and [begin, end) byte range in the data
+    section, in write order."""
+    table, pos = {}, 0
     for name, a in tensors.items():
-        header[name] = {"dtype": _DT[a.dtype], "shape": list(a.shape), "data_offsets": [offset, offset + a.nbytes]}
-        offset += a.nbytes
-    h = hashlib.sha256(_layout(header))
-    for a in tensors.values():
-        h.update(memoryview(a).cast("B") if a.size else b"")
-    header["__metadata__"] = {"format": FORMAT, "version": VERSION, "apsi": "apsi_b200",
-                              "units": "{}", "qtensors": json.dumps(qts),
-                              "metadata": json.dumps({str(k): v for k, v in (metadata or {}).items()}, default=str),
-                              "sha256": h.hexdigest()}
-    hb = json.dumps(header, separators=(",", ":")).encode("utf-8")
-    hb += b" " * ((-len(hb)) % 8)
-    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
-    tmp = path + ".tmp"
-    with open(tmp, "wb") as fh:
-        fh.write(struct.pack("<Q", len(hb)))
-        fh.write(hb)
-        for a in tensors.values():
-            if a.size:
-                fh.write(memoryview(a).cast("B"))
-    os.replace(tmp, path)
+        table[name] = {"dtype": _DT[a.dtype], "shape": list(a.shape), "data_offsets": [pos, pos + a.nbytes]}
+        pos += a.nbytes
+    return table
+
+
+def _digest(table, chunks):
+    """SHA-256 over the canonical tensor table followed by the data bytes (``chunks`` in file order): the
+    checksum the container stores, so files written here and by the reference verify in both."""
+    h = hashlib.sha256(_layout(table))
+    for c in chunks:
+        h.update(c)
+    return h.hexdigest()
+
+
+def save_packed(path, params, metadata=None):
+    """Write a parameter tree (dicts / lists of arrays and packed QTensors) as one ``.apsim`` file.
+
+    The file is assembled under a temporary name in the target directory and renamed over ``path`` at the end,
+    so a reader never sees a half-written checkpoint."""
+    path = str(path) if str(path).endswith(".apsim") else str(path) + ".apsim"
+    tensors, qts = _entries(params)
+    table = _table(tensors)
+    blobs = [memoryview(a).cast("B") for a in tensors.values() if a.size]
+    meta = {"format": FORMAT, "version": VERSION, "apsi": "apsi_b200", "units": "{}", "qtensors": json.dumps(qts),
+            "metadata": json.dumps({str(k): v for k, v in (metadata or {}).items()}, default=str),
+            "sha256": _digest(table, blobs)}
+    head = json.dumps(dict(table, __metadata__=meta), separators=(",", ":")).encode("utf-8")
+    head = head.ljust(len(head) + (8 - len(head) % 8) % 8, b" ")    # data section 8-byte aligned
+    folder = os.path.dirname(os.path.abspath(path))
+    os.makedirs(folder, exist_ok=True)
+    fd, tmp = tempfile.mkstemp(prefix=".apsim-", dir=folder)
+    try:
+        with os.fdopen(fd, "wb") as out:
+            out.write(len(head).to_bytes(8, "little"))
+            out.write(head)
+            for b in blobs:
+                out.write(b)
+        os.replace(tmp, path)
+    except BaseException:
+        if os.path.exists(tmp):
+            os.unlink(tmp)
+        raise
     return path
 
 
-def _read(path, verify):
-    bad = f"{os.path.basename(path)} is not a valid Apsi checkpoint"
-    if os.path.getsize(path) < 8:
-        raise RuntimeErr(bad + " (too short)")
-    mm = np.memmap(path, dtype=np.uint8, mode="r")
-    n = int(np.frombuffer(mm[:8], "<u8")[0])
-    if n > min(len(mm) - 8, 100 << 20):
-        raise RuntimeErr(bad + " (header size out of range)")
-    try:
-        header = json.loads(bytes(mm[8:8 + n]).decode("utf-8"))
-    except (UnicodeDecodeError, ValueError):
-        raise RuntimeErr(bad + " (unreadable header)")
-    meta = header.pop("__metadata__", {})
-    start = 8 + n
-    for name, info in header.items():
+class _Container:
+    """Reader of one ``.apsim`` file: parses and checks the header when opened, verifies the checksum on
+    request, and reads tensors by name."""
+
+    def __init__(self, path):
+        self.path = path
+        self.name = os.path.basename(path)
+        size = os.path.getsize(path)
+        with open(path, "rb") as fh:
+            raw = fh.read(8)
+            hlen = int.from_bytes(raw, "little") if len(raw) == 8 else -1
+            if hlen < 2 or hlen > min(size - 8, _MAX_HEADER):
+                self._fail("its header length field is missing or larger than the file")
+            text = fh.read(hlen)
         try:
-            a, b = (int(x) for x in info["data_offsets"])
-            dt = _DT_R[info["dtype"]]
-            count = int(np.prod([int(d) for d in info["shape"]], dtype=np.int64))
-        except (KeyError, TypeError, ValueError):
-            raise RuntimeErr(bad + f" (tensor '{name}' is described incorrectly)")
-        if not 0 <= a <= b <= len(mm) - start or b - a != count * dt.itemsize:
-            raise RuntimeErr(bad + f" (tensor '{name}' lies outside the file)")
-    if verify and "sha256" in meta:
-        h = hashlib.sha256(_layout(header))
-        end = start + max((v["data_offsets"][1] for v in header.values()), default=0)
-        for p in range(start, end, 1 << 26):
-            h.update(mm[p:min(end, p + (1 << 26))])
-        if h.hexdigest() != meta["sha256"]:
-            raise RuntimeErr(f"{os.path.basename(path)} is damaged or was modified: its data does not match the "
-                             f"SHA-256 stored in the file")
-    arrays = {}
-    for name, info in header.items():
-        a, b = info["data_offsets"]
-        dt = _DT_R[info["dtype"]]
-        arrays[name] = np.frombuffer(mm, dt, count=(b - a) // dt.itemsize, offset=start + a).reshape(info["shape"])
-    return arrays, meta
+            head = json.loads(text.decode("utf-8"))
+        except (UnicodeDecodeError, ValueError):
+            head = None
+        if not isinstance(head, dict):
+            self._fail("its header is not a JSON object")
+        self.meta = head.pop("__metadata__", {}) or {}
+        self.table = head
+        self.base = 8 + hlen
+        self.data_end = 0
+        room = size - self.base
+        self.layout = {}
+        for tname, info in head.items():
+            try:
+                dt = _DT_R[info["dtype"]]
+                shape = tuple(int(d) for d in info["shape"])
+                lo, hi = (int(v) for v in info["data_offsets"])
+            except (KeyError, TypeError, ValueError):
+                self._fail(f"the header entry of '{tname}' has no valid dtype, shape or data_offsets")
+            want = int(np.prod(shape, dtype=np.int64)) * dt.itemsize if shape else dt.itemsize
+            if min(shape, default=0) < 0 or lo < 0 or hi > room or hi - lo != want:
+                self._fail(f"the byte range of '{tname}' does not fit its shape or the file")
+            self.layout[tname] = (dt, shape, lo)
+            self.data_end = max(self.data_end, hi)
+
+    def _fail(self, why):
+        raise RuntimeErr(f"{self.name} cannot be read as an Apsi checkpoint: {why}")
+
+    def verify(self):
+        """Recompute the stored SHA-256 (when there is one) over the table and the data section."""
+        want = self.meta.get("sha256")
+        if not want:
+            return
+
+        def chunks():
+            left = self.data_end
+            with open(self.path, "rb") as fh:
+                fh.seek(self.base)
+                while left > 0:
+                    b = fh.read(min(_CHUNK, left))
+                    if not b:
+                        break
+                    left -= len(b)
+                    yield b
+        if _digest(self.table, chunks()) != want:
+            raise RuntimeErr(f"{self.name}: checksum (SHA-256) mismatch -- the tensor data or table changed after "
+                             f"the file was written")
+
+    def arrays(self):
+        """Every tensor as a read-only array mapped from the file."""
+        out = {}
+        for tname, (dt, shape, lo) in self.layout.items():
+            count = int(np.prod(shape, dtype=np.int64)) if shape else 1
+            if count == 0:
+                out[tname] = np.empty(shape, dt)
+                continue
+            out[tname] = np.memmap(self.path, dtype=dt, mode="r", offset=self.base + lo, shape=shape)
+        return out
+
+
+def _read(path, verify):
+    c = _Container(path)
+    if verify:
+        c.verify()
+    return c.arrays(), c.meta
 
 
 def load_packed(path, verify=True, device=None):

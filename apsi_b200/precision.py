@@ -436,8 +436,48 @@ def quant_error(x, fmt, axis=0, group=None):
     return math.sqrt(float(np.mean((r - xv) ** 2))) / denom
 
 
+# exponent bits, mantissa bits, bias, no infinities, top code of the top binade is NaN: the OCP fp8 and MX fp6 /
+# fp4 element formats (the reference's table, apsi/precision.py:65-72)
+_MF_SPEC = {"fp8_e4m3": (4, 3, 7, True, True), "fp8_e5m2": (5, 2, 15, False, False),
+            "fp6_e3m2": (3, 2, 3, True, False), "fp6_e2m3": (2, 3, 1, True, False),
+            "fp4_e2m1": (2, 1, 1, True, False)}
+
+
+def _minifloat_magnitudes(name):
+    """Value of every sign-less code of a minifloat format (inf / NaN where the format has them)."""
+    E, Mb, bias, finite_only, nan_top = _MF_SPEC[name]
+    code = np.arange(1 << (E + Mb))
+    e, m = code >> Mb, code & ((1 << Mb) - 1)
+    frac = m / float(1 << Mb)
+    v = np.where(e == 0, frac * 2.0 ** (1 - bias), (1.0 + frac) * 2.0 ** (e - bias))
+    top = e == (1 << E) - 1
+    if not finite_only:
+        v = np.where(top, np.where(m == 0, np.inf, np.nan), v)
+    if nan_top:
+        v = np.where(top & (m == (1 << Mb) - 1), np.nan, v)
+    return v
+
+
 def format_info(fmt):
-    f = get_format(fmt)
+    """name, bits, largest finite value, relative spacing (eps) and smallest positive value of a format
+    (apsi/precision.py:319-331); minifloats also give the number of distinct finite values.  Accepts every
+    name the reference knows, including the formats whose quantisation is not on the B200 path."""
+    name = getattr(fmt, "name", fmt)
+    name = ALIASES.get(name, name)
+    native = {"f64": np.float64, "f32": np.float32, "f16": np.float16}
+    if name in native:
+        fi = np.finfo(native[name])
+        return {"name": name, "bits": fi.bits, "max": float(fi.max), "eps": float(fi.eps), "tiny": float(fi.tiny)}
+    if name == "bf16":
+        return {"name": "bf16", "bits": 16, "max": 3.3895313892515355e38, "eps": 2.0 ** -7, "tiny": 2.0 ** -126}
+    if name == "uint8":
+        return {"name": "uint8", "bits": 8, "max": 255.0, "eps": 1.0, "tiny": 1.0}
+    f = get_format(name)
+    if f.kind == "minifloat":
+        v = _minifloat_magnitudes(f.name)
+        fin = v[np.isfinite(v)]
+        return {"name": f.name, "bits": f.bits, "max": f.max, "eps": 2.0 ** -_MF_SPEC[f.name][1],
+                "tiny": float(fin[fin > 0].min()), "values": int(fin.size * 2 - 1)}
     return {"name": f.name, "bits": f.bits, "max": f.max, "eps": 1.0, "tiny": 1.0}
 
 

@@ -238,9 +238,12 @@ int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes
  * device array per device instead (nothing in it needs to start at zero).  For callers that cannot allocate
  * at the call: engines whose free HBM is all handed to their own pool, loops that must not take the
  * synchronisation of cudaMalloc/cudaFree, bindings with no device allocator.  Shapes whose workspace exceeds
- * LB_NOALLOC_SCRATCH_BYTES fail with LB_E_WORKSPACE.  Calls that overlap in time on one device (two streams
- * or threads) race on the shared scratch; calls in order on one stream are safe.  The first call on a device
- * looks the scratch address up: make it outside stream capture.  No counterpart in the reference. */
+ * LB_NOALLOC_SCRATCH_BYTES fail with LB_E_WORKSPACE.  The array is reserved on every device where the library's
+ * kernels are loaded (whether or not this entry point is called) and held until the process exits.  Calls
+ * that overlap in time on one device (two streams or threads) race on the shared scratch; calls in order on one
+ * stream are safe.  The scratch address is looked up on the first call in each CUDA context of a device (the
+ * primary context, or a context made current through the driver API; a context re-created after
+ * cudaDeviceReset counts as new): make that call outside stream capture.  No counterpart in the reference. */
 int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                       int64_t N, const void* bias, int accumulate, void* y, int64_t ldy, void* stream);
 

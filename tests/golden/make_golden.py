@@ -1,9 +1,8 @@
 """Write the golden vectors that pin the oracle and the kernels to the reference.
 
-Run where the reference is importable (``APSI_REF`` names the directory that holds its ``apsi`` package;
-without it, the reference checkout of the build container is used):
+Run where the reference is importable; ``APSI_REF`` must name the directory that holds its ``apsi`` package:
 
-    python tests/golden/make_golden.py
+    APSI_REF=<reference checkout> python tests/golden/make_golden.py
 
 The outputs come from the reference's own functions -- ``apsi.precision.quantize`` / ``dequantize`` /
 ``qmatmul``, ``apsi.hub_gpu.qnumpy``, ``apsi.lowbit.round_weights`` and, for ``ref_packed.apsim``,
@@ -20,7 +19,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _reference():
-    root = os.environ.get("APSI_REF", "/root/reference")
+    root = os.environ.get("APSI_REF")
+    if not root or not os.path.isdir(os.path.join(root, "apsi")):
+        raise SystemExit("set APSI_REF to the directory that holds the reference's apsi package")
     sys.path.insert(0, root)
     from apsi import precision, hub_gpu  # noqa: E402
     return precision, hub_gpu
@@ -201,5 +202,39 @@ def main():
     print("wrote", path, {k: v.shape for k, v in out.items()})
 
 
+def precision_api(precision, path=None):
+    """Golden values of the precision module's metrics and tables (``round_to``, ``quant_error``,
+    ``format_info``, ``module``; apsi/precision.py:278-339) on seeded inputs, in precision_api_golden.npz."""
+    rng = np.random.default_rng(20261202)
+    x = (rng.standard_normal((24, 256)) * 0.05).astype(np.float32)
+    x[3, :] = 0.0                                        # an all-zero row (scale 1.0)
+    x[5, 17] = 2.5                                       # an outlier
+    out = {"x": x}
+    cases = [("int8", 0), ("fp8_e4m3", 0), ("fp8_e5m2", 0), ("fp6_e3m2", 0), ("fp6_e2m3", 0), ("fp4_e2m1", 0),
+             ("fp8_e4m3", None), ("fp4_e2m1", None)]
+    for fmt, axis in cases:
+        tag = f"{fmt}_{'row' if axis == 0 else 'tensor'}"
+        out["round_to_" + tag] = np.asarray(precision.round_to(x, fmt, "auto", axis), np.float64)
+        out["quant_error_" + tag] = np.float64(precision.quant_error(x, fmt, axis))
+    g = x.reshape(-1, 128)                               # int4 in groups of 128: the reference's own spelling
+    out["round_to_int4_g128"] = np.asarray(precision.round_to(g, "int4", "auto", 0), np.float64).reshape(x.shape)
+    out["quant_error_int4_g128"] = np.float64(precision.quant_error(g, "int4", 0))
+    names = ["int8", "int4", "fp8_e4m3", "fp8_e5m2", "fp6_e3m2", "fp6_e2m3", "fp4_e2m1", "f64", "f32", "f16",
+             "bf16", "uint8"]
+    info = np.zeros((len(names), 5), np.float64)
+    for i, n in enumerate(names):
+        r = precision.format_info(n)
+        info[i] = [r.bits, r.max, r.eps, r.tiny, getattr(r, "values", -1)]
+    out["format_info_names"] = np.array(names)
+    out["format_info"] = info
+    funcs = [k for k, v in precision.module().items() if callable(v) and k in
+             ("quantize", "dequantize", "round_to", "qmatmul", "nbytes", "quant_error", "format_info")]
+    out["module_functions"] = np.array(sorted(funcs))
+    path = path or os.path.join(HERE, "precision_api_golden.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path)
+
+
 if __name__ == "__main__":
     main()
+    precision_api(_reference()[0])

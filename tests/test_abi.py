@@ -117,3 +117,34 @@ def test_python_layer_raises_loudly_without_a_device():
                  lambda: kernels.act_mul(torch.zeros(2, 256, dtype=torch.bfloat16), 128)):
         with pytest.raises(_lib.LowbitError):      # host tensors: refused, never computed on the CPU
             call()
+
+
+def test_product_operand_checks_reject_short_or_wrong_outputs():
+    """kernels._check_product, run on host tensors: an output with too few rows or columns, the wrong dtype or a
+    column stride, and codes / scales / bias smaller than the format needs are rejected before any call."""
+    import torch
+    from apsi_b200 import kernels as Kn
+    M, N, K = 3, 64, 256
+    x = torch.zeros((M, K), dtype=torch.bfloat16)
+    codes = torch.zeros((N, K // 2), dtype=torch.uint8)
+    s16 = torch.zeros((N, K // 128), dtype=torch.float16)
+    ok = torch.zeros((M, N), dtype=torch.bfloat16)
+    Kn._check_product(_lib.FMT_INT4_G128, x, M, K, codes, s16, N, None, ok)            # fits
+    Kn._check_product(_lib.FMT_INT4_G128, x, M, K, codes, s16, N, None,
+                      torch.zeros((M, 2 * N), dtype=torch.bfloat16)[:, :N])              # strided rows: fine
+    bad_outs = [torch.zeros((M - 1, N), dtype=torch.bfloat16),                          # too few rows
+                torch.zeros((M, N - 1), dtype=torch.bfloat16),                          # too few columns
+                torch.zeros((M, N), dtype=torch.float32),                               # wrong dtype
+                torch.zeros((N, M), dtype=torch.bfloat16).t()]                          # column stride != 1
+    for out in bad_outs:
+        with pytest.raises(_lib.LowbitError) as e:
+            Kn._check_product(_lib.FMT_INT4_G128, x, M, K, codes, s16, N, None, out)
+        assert e.value.code == _lib.LB_E_ARG
+    with pytest.raises(_lib.LowbitError, match="codes holds"):
+        Kn._check_product(_lib.FMT_INT4_G128, x, M, K, codes[:-1], s16, N, None, ok)
+    with pytest.raises(_lib.LowbitError, match="scales holds"):
+        Kn._check_product(_lib.FMT_INT8_ROW, x, M, K, torch.zeros((N, K), dtype=torch.int8),
+                          torch.zeros((N - 1,), dtype=torch.float16), N, None, ok)
+    with pytest.raises(_lib.LowbitError, match="bias"):
+        Kn._check_product(_lib.FMT_INT4_G128, x, M, K, codes, s16, N, torch.zeros((N - 1,), dtype=torch.bfloat16),
+                          ok)

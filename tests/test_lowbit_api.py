@@ -83,3 +83,41 @@ def test_matmul_dispatches_packed_weights_to_the_fused_kernels(cuda):
     assert torch.equal(y, P.qmatmul(xd, qt))
     dense = torch.randn((K, 8), device=cuda)
     assert torch.equal(lowbit.matmul(xd.float(), dense), xd.float() @ dense)
+
+
+@pytest.mark.gpu
+def test_dense_fp8_matmul_rounds_w_per_column_and_has_a_gradient(cuda):
+    """lowbit.matmul on a dense weight with the fp8 switch on: w rounded to e4m3 per output column (the oracle's
+    per-row minifloat quantiser on w^T), x exact in bfloat16; the bfloat16 backward of the reference."""
+    import torch
+    assert lowbit.fp8_matmul_available(cuda)
+    K, N, M = 512, 192, 5
+    x, Wt = ora.make_config_inputs(M, N, K, seed=31)          # Wt: [N, K]
+    codes, s = ora.quant_minifloat(Wt, "fp8_e4m3", axis=0)
+    ref = ora.linear_ref(x, ora.dequant_minifloat(codes, "fp8_e4m3", Wt.shape, s))
+    xd = torch.from_numpy(x).to(cuda).requires_grad_(True)
+    w = torch.from_numpy(Wt.T.copy()).to(cuda).requires_grad_(True)
+    old = lowbit._HW["on"]
+    lowbit._HW["on"] = True
+    try:
+        y = lowbit.matmul(xd, w)
+    finally:
+        lowbit._HW["on"] = old
+    assert y.dtype == torch.bfloat16 and y.shape == (M, N)
+    yn = y.detach().float().cpu().numpy()
+    assert ora.rel_frobenius(yn, ref) <= 2e-3 and ora.max_abs_ratio(yn, ref) <= 1e-2
+    g = torch.randn((M, N), device=cuda)
+    y.backward(g)
+    gb = g.to(torch.bfloat16)
+    assert torch.equal(xd.grad, (gb @ w.detach().to(torch.bfloat16).t()).float())
+    assert torch.equal(w.grad, (xd.detach().to(torch.bfloat16).t() @ gb).float())
+    # off: the ordinary product
+    assert torch.equal(lowbit.matmul(xd.detach(), w.detach()), xd.detach() @ w.detach())
+
+
+def test_fp8_matmul_available_honours_the_switch(monkeypatch):
+    import torch
+    monkeypatch.setenv("APSI_FP8_MATMUL", "0")
+    assert lowbit.fp8_matmul_available(torch.device("cuda", 0)) is False
+    monkeypatch.setenv("APSI_FP8_MATMUL", "1")
+    assert lowbit.fp8_matmul_available(torch.device("cpu")) is False
