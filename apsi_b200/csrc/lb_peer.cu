@@ -12,7 +12,8 @@
 // lb_peer_close on the other ranks, lb_peer_free by the owner.
 //
 // Barrier: each rank owns an array of G 32-bit flags in a peer buffer.  lb_rank_barrier(epoch) runs after the
-// products in stream order; its system-scope fence and release stores order every store of those kernels
+// products in stream order, launched as their programmatic dependent (so the next static-weight product streams
+// its weights while the barrier waits); its system-scope fence and release stores order every store of those kernels
 // (local and peer) before the flag it writes into slot `rank` of every rank's array, and it waits until every
 // slot of its own array has reached `epoch` (acquire loads), i.e. every rank's stores are visible here.  The
 // wait gives up after a time limit, sets LB_DEVERR_PEER_TIMEOUT in the device error word and returns, so a
@@ -44,6 +45,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 __global__ void rank_barrier_kernel(const BarrierParams p) {
+  // Launched as a programmatic dependent of the products: the next kernel on the stream (the following
+  // static-weight GEMV) may launch now and stream its weights while this barrier waits for the other ranks;
+  // everything it reads from earlier kernels waits for this grid to complete.  griddepcontrol.wait below
+  // returns once the products before this barrier have completed and their stores are performed.
+  pdl_launch_dependents();
+  pdl_wait();
   if (threadIdx.x != 0) return;
   uint32_t* mine = p.flags[p.rank];
   uint32_t epoch = p.epoch;
@@ -160,8 +167,17 @@ int lb_rank_barrier(uint32_t* const* flags_ranks, int G, int rank, uint32_t epoc
   DevInfo* d;
   int r = current(&d);
   if (r) return r;
-  rank_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return launched(cudaGetLastError(), "rank_barrier");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return launched(cudaLaunchKernelEx(&cfg, rank_barrier_kernel, p), "rank_barrier");
 }
 
 }  // extern "C"

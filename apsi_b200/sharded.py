@@ -107,6 +107,10 @@ class PeerOutputs:
         b = (self.epoch + 1) & 1
         return self.ptrs[b], self._views[b][:M]
 
+    def view0(self, M):
+        """The local [M, N] view of output buffer 0 (the one a caller that passes ``ptrs[0]`` itself writes)."""
+        return self._views[0][:M]
+
     def finish(self):
         """Barrier: every rank's stores of this call are visible on every rank (on the current stream).  The
         barrier's epoch comes from the device-side counter, so the call may be captured in a CUDA graph."""

@@ -325,6 +325,12 @@ def run_ours(args, rank, world, local_rank):
                             "ms": round(float(ag), 4), "bytes_received_per_rank": per_rank,
                             "GB_per_s_per_rank": round(per_rank / (float(ag) * 1e-3) / 1e9, 2)}
 
+    if world > 1:                          # layer 0's fused gather against an NCCL all-gather of the shards
+        out["gather_bitexact"] = gather_check(
+            torch, Kn, FMT_INT4_G128, dev, rank, world, [(packed[0], scales[0], N1, K1)], {K1: x}, [ys[0]],
+            [torch.empty((world, M1, N1), dtype=torch.bfloat16, device=dev)],
+            [(peers.ptrs[0], peers.ptrs[2], N1 * world, peers.view0(M1))], M1)
+
     # ---- e2e through the public API: pinned host x in, every layer's y back to pinned host memory
     qts = []
     for i in range(LAYERS):
@@ -442,6 +448,15 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
         mats.append(lst)
     total_w = sum(weight_bytes(n, k) for _, n, k in shapes)
     flops_per_token = 2 * sum(n * k for _, n, k in shapes)
+    # world > 1: the whole (unsharded) MLP on each GPU alone, the 1-GPU time the strong-scaling efficiency of
+    # this run is computed against (363 MB of weights, more than twice the L2: one copy suffices)
+    full_mats = []
+    if world > 1:
+        for _, n, k in shapes:
+            W = torch.randn((n, k), generator=gen, device=dev) * 0.015
+            p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+            del W
+            full_mats.append((p, s16, n, k))
 
     def maxed(v):
         t = torch.tensor([v], dtype=torch.float64, device=dev)
@@ -464,6 +479,12 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
             for j, (p, s16, nl, k) in enumerate(mats[c]):
                 Kn.linear(fmt, xs[k], p, s16, nl, out=ys[j], static_weights=(M <= 16))
 
+        yfull = [torch.empty((M, n), dtype=torch.bfloat16, device=dev) for (_, _, n, _) in full_mats]
+
+        def single():
+            for j, (p, s16, n, k) in enumerate(full_mats):
+                Kn.linear(fmt, xs[k], p, s16, n, out=yfull[j], static_weights=(M <= 16))
+
         def gather():
             for j in range(3):
                 dist.all_gather_into_tensor(gath[j].view(-1), ys[j].view(-1))
@@ -481,8 +502,10 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                 if world > 1:
                     gather()
                     fused(c)
+            if world > 1:
+                single()
         torch.cuda.synchronize(dev)
-        graph = fgraph = None
+        graph = fgraph = sgraph = None
         if M <= 16:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
@@ -493,8 +516,11 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                 with torch.cuda.graph(fgraph, stream=stream):
                     for c in range(copies):
                         fused(c)
+                sgraph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(sgraph, stream=stream):
+                    single()
             torch.cuda.synchronize(dev)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(10)]
         if world > 1:
             dist.barrier()
         with torch.cuda.stream(stream):
@@ -525,6 +551,13 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                         for c in range(copies):
                             fused(c)
                 ev[7].record(stream)
+                ev[8].record(stream)
+                for _ in range(reps * copies):
+                    if sgraph is not None:
+                        sgraph.replay()
+                    else:
+                        single()
+                ev[9].record(stream)
         torch.cuda.synchronize(dev)
         n_mlp = reps * copies
         comp_s = maxed(ev[0].elapsed_time(ev[1]) * 1e-3 / n_mlp)
@@ -551,13 +584,41 @@ def mlp70b_measure(torch, Kn, fmt, dev, rank, world, stream, hbm_peak, tf_peak, 
                 r["fused_weight_GB_per_s"] = round(total_w / fu_s / 1e9, 1)
             else:
                 r["fused_TFLOP_per_s"] = round(flops_per_token * M / fu_s / 1e12, 1)
+            one_s = maxed(ev[8].elapsed_time(ev[9]) * 1e-3 / n_mlp)
+            r["single_gpu_us_per_mlp"] = round(one_s * 1e6, 2)
+            r["compute_efficiency"] = round(one_s / (world * comp_s), 4)
+            r["fused_efficiency"] = round(one_s / (world * fu_s), 4)
+        if world > 1:
+            r["gather_bitexact"] = gather_check(torch, Kn, fmt, dev, rank, world, mats[0], xs, ys, gath,
+                                                [(q.ptrs[0], q.ptrs[2], q.N, q.view0(M)) for q in peers], M)
         res[f"M={M}"] = r
-        del graph, fgraph
+        del graph, fgraph, sgraph
     res["peaks"] = f"{peak_kind} hbm_gbs {hbm_peak} and bf16_tflops {tf_peak}, times world size"
     if peers is not None:
         for q in peers:
             q.close()
     return res
+
+
+def gather_check(torch, Kn, fmt, dev, rank, world, mats, xs, ys, gath, outs, M):
+    """Correctness of the fused gather at this world size, checked by the bench itself: every rank runs each
+    product once more with the gather fused in (peer stores + flag barrier), then computes its own shard alone,
+    collects all ranks' shards with an NCCL all-gather + interleave, and compares that [M, N] with the fused
+    output bit for bit.  True only if every matrix matches on every rank."""
+    import torch.distributed as dist
+    ok = True
+    for j, (p, s16, nl, k) in enumerate(mats):
+        yptrs, fptrs, ldy, view = outs[j]
+        Kn.linear_sharded(fmt, xs[k], p, s16, nl, yptrs, rank, ldy, static_weights=(M <= 16))
+        Kn.rank_barrier(fptrs, rank, 0, dev)
+        Kn.linear(fmt, xs[k], p, s16, nl, out=ys[j])
+        dist.all_gather_into_tensor(gath[j].view(-1), ys[j].view(-1))
+        ref = Kn.interleave_cols(gath[j], world, M, nl)
+        torch.cuda.synchronize(dev)
+        ok = ok and bool(torch.equal(view, ref))
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(int(t) == 1) and Kn.device_errors(dev) == 0
 
 
 def decoder_measure(torch, dev, hbm_peak, batch=8, prompt=512, steps=128):
