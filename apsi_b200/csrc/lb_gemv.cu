@@ -44,6 +44,19 @@
 #include "lb_kernels.h"
 #include "lb_tmap.h"
 
+#ifndef LB_GEMV_BOX_G
+#define LB_GEMV_BOX_G 3          // box mode (int4, M <= 2): consumer groups per CTA
+#endif
+#ifndef LB_GEMV_BOX_MINB
+#define LB_GEMV_BOX_MINB 1       // box mode: CTAs per SM the registers and shared memory are sized for
+#endif
+#ifndef LB_GEMV_BOX_LR
+#define LB_GEMV_BOX_LR false     // box mode: codes read from the slot unit by unit (slot held until the multiply ends)
+#endif
+#ifndef LB_GEMV_BOX_SLOTS
+#define LB_GEMV_BOX_SLOTS 3      // box mode: most ring slots
+#endif
+
 namespace lb {
 
 namespace gemv {
@@ -1045,6 +1058,10 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
     if (e != cudaSuccess) return e;
+    // the whole unified L1 as shared memory, so that a CTA of the next launch (programmatic dependent launch)
+    // finds room beside a running one whenever the registers and the shared-memory footprint allow two
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   int limit = MINB >= 2 ? HALF_SM_SMEM : SMEM_LIMIT;
@@ -1188,7 +1205,8 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
       bool stma = false;
       if (encode_gemv_boxes(codes, scales, N, K, true, &tw, &ts, &stma)) {
         p.scale_tma = stma ? 1 : 0;
-        return launch_gemv_t<20, 1, 3, 1, true>(p, sms, 1, 3, pdl, st, &tw, &ts);
+        return launch_gemv_t<20, 1, LB_GEMV_BOX_G, LB_GEMV_BOX_MINB, true, LB_GEMV_BOX_LR>(p, sms, 1, LB_GEMV_BOX_SLOTS,
+                                                                                          pdl, st, &tw, &ts);
       }
     }
 #endif

@@ -17,8 +17,8 @@ into every rank's full output over NVLink (CUDA IPC peer buffers), and one flag 
 inside the timed CUDA graph.  An NCCL all-gather of the same outputs is timed on its own for comparison.
 
 Also reported: the GEMV's live roofline (CUDA events on the launching stream), ``e2e`` through the public API
-(``apsi_b200.precision.qmatmul``) from pinned host memory and back, the reference CPU path (the oracle port of
-``precision.qmatmul``) as ``cpu_baseline``, the prefill GEMM of configs[2] (M=2048, N=12288, K=4096), and
+(``apsi_b200.precision.qmatmul``) from pinned host memory and back, the reference's fastest CPU path (hub_cpu's
+Q8_0 GEMV on all host cores, restated in ``oracle/hub_q8.c``) as ``cpu_baseline``, the prefill GEMM of configs[2] (M=2048, N=12288, K=4096), and
 ``mlp70b``: the 70B-shaped MLP of configs[4] column-sharded over all ranks (strong scaling) at M = 1, 64 and
 2048, with the per-rank products, the NCCL all-gathers and both together timed separately.
 """
@@ -138,9 +138,40 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------ CPU baseline
-def cpu_baseline_sample(reps=2):
-    """The reference's CPU path for an int4 product (precision.qmatmul = dequantise + float32 matmul,
-    restated in oracle/), on [11008, 4096] weights at M=1: packed-weight GB/s."""
+def _q8_layer(M, seed=0):
+    """configs[1]'s layer in the reference's Q8_0 CPU layout (bfloat16-rounded weights ~ N(0, 0.02)) and M
+    float32 tokens."""
+    import oracle as O
+    from oracle import hub_q8
+    rng = np.random.default_rng(seed)
+    W = O.bf16_round((rng.standard_normal((N1, K1)) * 0.02).astype(np.float32))
+    codes, scales = hub_q8.q8_from_weights(W)
+    x = O.bf16_round(rng.standard_normal((M, K1)).astype(np.float32))
+    return codes, scales, x
+
+
+def time_hub_q8(M, reps, warmup=2, threads=0):
+    """The reference's fastest CPU product (hub_cpu.matmul on Q8_0 weights, all cores), restated in
+    oracle/hub_q8.c, on configs[1]'s [11008, 4096] layer at M tokens: seconds per product (median of `reps`)."""
+    from oracle import hub_q8
+    codes, scales, x = _q8_layer(M)
+    for _ in range(warmup):
+        hub_q8.matmul(x, codes, scales, threads)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        hub_q8.matmul(x, codes, scales, threads)
+        ts.append(time.perf_counter() - t0)
+    return float(np.median(ts)), codes.nbytes + scales.nbytes
+
+
+def cpu_baseline_sample():
+    """cpu_baseline of our arm: the reference's fastest CPU path (hub_cpu's Q8_0 GEMV on all host cores,
+    restated in C) on configs[1]'s layer at M=1, as configs[1]-layer-equivalent GB/s (the int4-g128 bytes of the
+    same [11008, 4096] layer per second of the CPU product), plus the NumPy port of precision.qmatmul."""
+    from oracle import hub_q8
+    threads = hub_q8.host_threads()
+    dt, q8_bytes = time_hub_q8(1, reps=200, threads=threads)
     import oracle as O
     rng = np.random.default_rng(0)
     W = (rng.standard_normal((N1, K1)) * 0.02).astype(np.float32)
@@ -148,44 +179,56 @@ def cpu_baseline_sample(reps=2):
     x = O.bf16_round(rng.standard_normal((M1, K1)).astype(np.float32))
     O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")        # warm
     t0 = time.perf_counter()
-    for _ in range(reps):
-        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
-    dt = (time.perf_counter() - t0) / reps
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:                          # noqa: BLE001
-        cores = os.cpu_count()
-    return weight_bytes(N1, K1) / dt / 1e9, dt, cores
+    O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
+    dn = time.perf_counter() - t0
+    return {"value": round(weight_bytes(N1, K1) / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"200 products of configs[1]'s [11008,4096] layer at M=1 through oracle/hub_q8.c, the C "
+                      f"restatement of hub_cpu.matmul on Q8_0 weights (the reference's fastest CPU path; its "
+                      f"thread team over {threads} threads): {dt * 1e3:.3f} ms per product, "
+                      f"{q8_bytes / dt / 1e9:.1f} GB/s of Q8_0 bytes; value = int4-g128 bytes of the same layer "
+                      f"per second",
+            "numpy_qmatmul": {"ms_per_product": round(dn * 1e3, 1),
+                              "value": round(weight_bytes(N1, K1) / dn / 1e9, 4),
+                              "what": "oracle port of precision.qmatmul (dequantise + float32 BLAS), 1 product"}}
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's fastest CPU product for this layer -- hub_cpu.matmul on Q8_0 weights
+    over all host cores (restated in oracle/hub_q8.c; the reference's own code cannot run on the GPU machines) --
+    on configs[1]'s [11008, 4096] layer at M=1, one product per step.  ``value`` is configs[1]-layer-equivalent
+    GB/s (the int4-g128 bytes of the same layer per second), so the ratio of the two arms is the ratio of their
+    times per product; the Q8_0 byte rate is reported beside it, with M = 4 and 16."""
     if rank != 0:
         return 0
-    import oracle as O
-    rng = np.random.default_rng(0)
-    W = (rng.standard_normal((N1, K1)) * 0.02).astype(np.float32)
-    packed, _, s16 = O.quant_int4_g128(W)
-    x = O.bf16_round(rng.standard_normal((M1, K1)).astype(np.float32))
-    for _ in range(args.warmup):
-        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
-    t0 = time.perf_counter()
+    from oracle import hub_q8
+    threads = hub_q8.host_threads()
+    codes, scales, x = _q8_layer(M1)
+    for _ in range(max(args.warmup, 1)):
+        hub_q8.matmul(x, codes, scales, threads)
+    ts = []
     for _ in range(args.steps):
-        O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
-    dt = (time.perf_counter() - t0) / args.steps
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:                          # noqa: BLE001
-        cores = os.cpu_count()
+        t0 = time.perf_counter()
+        hub_q8.matmul(x, codes, scales, threads)
+        ts.append(time.perf_counter() - t0)
+    dt = float(np.sum(ts)) / args.steps
     val = weight_bytes(N1, K1) / dt / 1e9
-    sample = "one [11008,4096] int4-g128 product per step (M=1): dequantise (NumPy) + float32 matmul (BLAS)"
+    q8b = codes.nbytes + scales.nbytes
+    per_m = {}
+    for M in (4, 16):
+        dm, _ = time_hub_q8(M, reps=max(5, args.steps // 4), threads=threads)
+        per_m[f"M={M}"] = {"ms_per_product": round(dm * 1e3, 4), "value": round(weight_bytes(N1, K1) / dm / 1e9, 3),
+                           "q8_weight_GB_per_s": round(q8b / dm / 1e9, 2)}
+    sample = (f"one product of configs[1]'s [11008,4096] layer per step at M=1 through oracle/hub_q8.c, the C "
+              f"restatement of hub_cpu.matmul on Q8_0 weights with its thread team over {threads} threads")
     out = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "configs[1]: int4-g128 GEMV M=1, W[11008,4096] (bounded sample: 1 layer per step)",
-                      "M": M1, "N": N1, "K": K1, "path": "oracle port of precision.qmatmul (CPU)"},
-           "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32->f32", "data": "synthetic",
+           "config": {"workload": "configs[1]: decode product M=1 of the [11008,4096] layer, one per step "
+                                  "(value: int4-g128 bytes of that layer per second of the CPU product)",
+                      "M": M1, "N": N1, "K": K1,
+                      "path": "hub_cpu.matmul on Q8_0 (apsi/hub_cpu.py:96-194, 404-534), restated in C",
+                      "q8_weight_GB_per_s": round(q8b / dt / 1e9, 2), "per_M": per_m},
+           "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                             "sample": sample},
            "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
@@ -377,10 +420,7 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0 and world == 1:
         try:
-            v, dt, cores = cpu_baseline_sample()
-            out["cpu_baseline"] = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                                   "sample": f"2 products of [11008,4096] int4-g128 at M=1 via the oracle port of "
-                                             f"precision.qmatmul ({dt * 1e3:.0f} ms each)"}
+            out["cpu_baseline"] = cpu_baseline_sample()
         except Exception as e:               # noqa: BLE001
             out["cpu_baseline"] = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
                                    "sample": f"failed: {type(e).__name__}: {e}"}

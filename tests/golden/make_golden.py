@@ -235,6 +235,32 @@ def precision_api(precision, path=None):
     print("wrote", path)
 
 
+def hub_cpu_q8(path=None):
+    """Golden outputs of the reference's fastest CPU product (``apsi.hub_cpu``: ``Q8.from_bf16`` and ``matmul``
+    on a Q8, apsi/hub_cpu.py:170-194, 474-534) on seeded bfloat16 weights, in hub_q8_golden.npz.  They pin
+    the C restatement ``oracle/hub_q8.c`` that bench.py times as the CPU baseline."""
+    from apsi import hub_cpu  # noqa: E402  (after _reference() put the reference on the path)
+    if not hub_cpu.q8_available():
+        raise SystemExit("the reference's native Q8 product is not available here")
+    rng = np.random.default_rng(3202)
+    out = {}
+    for tag, (O, I, T) in {"a": (300, 512, 3), "b": (256, 1024, 1), "c": (64, 2048, 16)}.items():
+        W = (rng.standard_normal((O, I)) * 0.02).astype(np.float32)
+        W[7, :64] = 0.0                                  # an all-zero block (scale 0, codes 0)
+        bits = (W.view(np.uint32) >> np.uint32(16)).astype(np.uint16)       # bfloat16 by truncation
+        q = hub_cpu.Q8.from_bf16(bits)
+        x = rng.standard_normal((T, I)).astype(np.float32)
+        if tag == "a":                                   # the quantiser's input, for the Q8_0 code check
+            out[f"{tag}_wbits"] = bits
+        out[f"{tag}_codes"], out[f"{tag}_scales"] = q.codes, q.scales
+        out[f"{tag}_x"] = x
+        out[f"{tag}_y"] = np.asarray(hub_cpu.matmul(x, q), np.float32)
+    path = path or os.path.join(HERE, "hub_q8_golden.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path)
+
+
 if __name__ == "__main__":
     main()
     precision_api(_reference()[0])
+    hub_cpu_q8()
