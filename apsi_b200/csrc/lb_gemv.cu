@@ -44,19 +44,6 @@
 #include "lb_kernels.h"
 #include "lb_tmap.h"
 
-#ifndef LB_GEMV_BOX_G
-#define LB_GEMV_BOX_G 3          // box mode (int4, M <= 2): consumer groups per CTA
-#endif
-#ifndef LB_GEMV_BOX_MINB
-#define LB_GEMV_BOX_MINB 1       // box mode: CTAs per SM the registers and shared memory are sized for
-#endif
-#ifndef LB_GEMV_BOX_LR
-#define LB_GEMV_BOX_LR false     // box mode: codes read from the slot unit by unit (slot held until the multiply ends)
-#endif
-#ifndef LB_GEMV_BOX_SLOTS
-#define LB_GEMV_BOX_SLOTS 3      // box mode: most ring slots
-#endif
-
 namespace lb {
 
 namespace gemv {
@@ -536,34 +523,48 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
       } else if (FMT == 20) {
         // int4 on the integer path: per (token, unit) e with max|x| * 2^-e in [2^13, 2^14), x16 = rint(x * 2^-e), split into signed
         // bytes hi = (x16 + 128) >> 8 and lo = x16 - 256 hi, written in the B-fragment order of the m16n8k32
-        // tiles (column 2t: hi, 2t + 1: lo of token t); the offset correction 8 * sum(digit) per (token, unit)
+        // tiles (column 2t: hi, 2t + 1: lo of token t); the offset correction 8 * sum(digit) per (token, unit).
+        // One half-warp per (token, unit): lane j of the half takes the unit's 16-byte chunk j, so the unit's
+        // absmax and digit sums are 4-step shuffle trees inside the half.  A warp issues the loads of its pairs
+        // of SB passes before any arithmetic, and a pass with no pair for the warp is skipped (this path runs
+        // for M <= 2, where a CTA stages at most 2 x 32 units per K range).
         int* corr_i = reinterpret_cast<int*>(corr);                       // [M][units][2]
         float* fac = corr + 2 * p.M * units_staged;                       // [M][units] 2^e
-        for (int base = 0; base < nch; base += CT * XB) {
-          uint4 v[XB];
-          RmsW wv[XB];
+        constexpr int PPI = 2 * NCW;                                      // pairs per pass: two per warp
+        constexpr int SB = 2;                                             // passes with loads in flight together
+        const int npair = p.M * units_staged;
+        const int j = lane & 15;
+        for (int base = 2 * warp; base < npair; base += PPI * SB) {      // warp-uniform
+          uint4 v[SB];
+          RmsW wv[SB];
+          int tv[SB], ilv[SB], jjv[SB];
+          bool okv[SB];
 #pragma unroll
-          for (int b = 0; b < XB; ++b) {
-            int t, il, jj, r;
+          for (int b = 0; b < SB; ++b) {
+            const int pi = base + b * PPI + (lane >> 4);
+            int t = 0, uloc = pi;
+            while (uloc >= units_staged) { uloc -= units_staged; ++t; }
+            const int il = uloc / RANGE_UNITS, u = uloc % RANGE_UNITS;
+            const int r = rank + il * R;
+            tv[b] = t; ilv[b] = il; jjv[b] = u * CPU + j;
+            okv[b] = pi < npair && r * RANGE_UNITS + u < p.total_units;
             v[b] = make_uint4(0u, 0u, 0u, 0u);
-            if (locate(base + b * CT + ctid, t, il, jj, r)) {
-              const int64_t k0 = static_cast<int64_t>(r) * RANGE_UNITS * KPU + jj * 8;
+            if (okv[b]) {
+              const int64_t k0 = static_cast<int64_t>(r) * RANGE_UNITS * KPU + jjv[b] * 8;
               v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + k0);
               if (p.ln) wv[b] = rms_load_w(p.ln, p.ln_f32 != 0, k0, p.K, p.ln_vec != 0);
             }
           }
           if (p.ln) {                            // norm prologue: bf16((x * fac) * (w + off)), as lb_rmsnorm
 #pragma unroll
-            for (int b = 0; b < XB; ++b) {
-              int t, il, jj, r;
-              if (locate(base + b * CT + ctid, t, il, jj, r)) v[b] = rms_apply_chunk(v[b], lnf[t], wv[b], p.ln_f32 != 0, p.ln_off);
-            }
+            for (int b = 0; b < SB; ++b)
+              if (okv[b]) v[b] = rms_apply_chunk(v[b], lnf[tv[b]], wv[b], p.ln_f32 != 0, p.ln_off);
           }
 #pragma unroll
-          for (int b = 0; b < XB; ++b) {
-            const int q = base + b * CT + ctid;
-            int t, il, jj, r;
-            const bool ok = locate(q, t, il, jj, r);
+          for (int b = 0; b < SB; ++b) {
+            if (base + b * PPI >= npair) break;                           // warp-uniform
+            const int t = tv[b], il = ilv[b], jj = jjv[b];
+            const bool ok = okv[b];
             const uint32_t rr[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
             float xf[8];
 #pragma unroll
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
             };
             if (ok) {
               const int uloc = il * RANGE_UNITS + (jj >> 4);
-              const int j = jj & 15, cq = j >> 2, i = j & 3;
+              const int jc = jj & 15, cq = jc >> 2, i = jc & 3;
               const int T = t >> 2, tt = t & 3;
               const int ncols = min(8, 2 * p.M - 8 * T);
               uint8_t* base_p = xs + T * units_staged * 1024 + uloc * (ncols * 128) + (i >> 1) * (ncols * 64) +
@@ -608,15 +609,17 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
               *reinterpret_cast<uint2*>(base_p + (2 * tt + 1) * 64) =
                   make_uint2(pack4(ld[0], ld[2], ld[4], ld[6]), pack4(ld[1], ld[3], ld[5], ld[7]));
             }
+            // both digit sums in one word: |sum hi| < 2^13 and |sum lo| < 2^15 over a unit, so
+            // 65536 sh + sl adds without overflow and its low half is sum lo as a signed 16-bit value
+            int both = sh * 65536 + sl;
 #pragma unroll
-            for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) {
-              sh += __shfl_xor_sync(0xffffffffu, sh, o2);
-              sl += __shfl_xor_sync(0xffffffffu, sl, o2);
-            }
-            if (ok && (jj % CPU) == 0) {
+            for (int o2 = CPU / 2; o2 >= 1; o2 >>= 1) both += __shfl_xor_sync(0xffffffffu, both, o2);
+            if (ok && (jj & 15) == 0) {
               const int uloc = il * RANGE_UNITS + (jj >> 4);
-              corr_i[(t * units_staged + uloc) * 2] = 8 * sh;
-              corr_i[(t * units_staged + uloc) * 2 + 1] = 8 * sl;
+              const int slo = static_cast<int16_t>(both & 0xFFFF);
+              const int shi = (both - slo) / 65536;
+              corr_i[(t * units_staged + uloc) * 2] = 8 * shi;
+              corr_i[(t * units_staged + uloc) * 2 + 1] = 8 * slo;
               fac[t * units_staged + uloc] = __int_as_float((127 + e) << 23);   // 2^e
             }
           }
@@ -1058,10 +1061,6 @@ static cudaError_t launch_gemv_t(GemvParams p, int sms, int ctas_per_sm, int max
   if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
     if (e != cudaSuccess) return e;
-    // the whole unified L1 as shared memory, so that a CTA of the next launch (programmatic dependent launch)
-    // finds room beside a running one whenever the registers and the shared-memory footprint allow two
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   int limit = MINB >= 2 ? HALF_SM_SMEM : SMEM_LIMIT;
@@ -1205,8 +1204,13 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
       bool stma = false;
       if (encode_gemv_boxes(codes, scales, N, K, true, &tw, &ts, &stma)) {
         p.scale_tma = stma ? 1 : 0;
-        return launch_gemv_t<20, 1, LB_GEMV_BOX_G, LB_GEMV_BOX_MINB, true, LB_GEMV_BOX_LR>(p, sms, 1, LB_GEMV_BOX_SLOTS,
-                                                                                          pdl, st, &tw, &ts);
+        // one or two K ranges per row and a row block for every SM: six slots, so a CTA requests (almost) its
+        // whole share of the weights at once, with the codes read from the slot unit by unit
+        // ([11008, 4096]: 7.15 -> 6.68 us, [28672, 8192]: 25.1 -> 23.4 us); otherwise three slots
+        // ([4096, 11008]: 10.2 against 11.0 us, [8192, 28672]: 31.7 against 49 us with six)
+        if (p.nr <= 2 && p.nblocks >= sms)
+          return launch_gemv_t<20, 1, 3, 1, true, true>(p, sms, 1, 6, pdl, st, &tw, &ts);
+        return launch_gemv_t<20, 1, 3, 1, true>(p, sms, 1, 3, pdl, st, &tw, &ts);
       }
     }
 #endif

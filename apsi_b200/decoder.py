@@ -92,13 +92,11 @@ class _Proj:
 class QuantDecoder:
     """The decoder of configs[3] with packed low-bit projections (see the module docstring)."""
 
+    _FMTS = {"int4": FMT_INT4_G128, "int8": FMT_INT8_ROW, "fp8_e4m3": FMT_FP8_E4M3, "fp4_e2m1": FMT_FP4_E2M1}
+
     def __init__(self, cfg=None, device="cuda", fmt="int4", seed=0, max_positions=8192):
-        self.cfg = cfg = cfg or DecoderConfig()
-        self.dev = torch.device(device)
-        fmts = {"int4": FMT_INT4_G128, "int8": FMT_INT8_ROW, "fp8_e4m3": FMT_FP8_E4M3, "fp4_e2m1": FMT_FP4_E2M1}
-        if fmt not in fmts:
-            raise LowbitError(LB_E_ARG, f"projection format '{fmt}' is not one of {sorted(fmts)}")
-        self.fmt = fmts[fmt]
+        self._setup(cfg or DecoderConfig(), device, fmt, max_positions)
+        cfg = self.cfg
         g = torch.Generator(device=self.dev)
         g.manual_seed(seed)
         width = (cfg.nh + 2 * cfg.kvh) * cfg.dh
@@ -122,11 +120,73 @@ class QuantDecoder:
             })
         self.norm = torch.ones(cfg.H, dtype=torch.bfloat16, device=self.dev)
         self.head = proj(cfg.V, cfg.H)
+
+    def _setup(self, cfg, device, fmt, max_positions):
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        if fmt not in self._FMTS:
+            raise LowbitError(LB_E_ARG, f"projection format '{fmt}' is not one of {sorted(self._FMTS)}")
+        self.fmt = self._FMTS[fmt]
         half = cfg.dh // 2
-        self._inv = 1.0 / (cfg.theta ** (torch.arange(half, device=self.dev, dtype=torch.float32) / half))
-        ang = torch.arange(max_positions, device=self.dev, dtype=torch.float32)[:, None] * self._inv[None, :]
-        self._cos, self._sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()   # [positions, dh / 2]
+        inv = 1.0 / (cfg.theta ** (torch.arange(half, device=self.dev, dtype=torch.float64) / half))
+        self._inv = inv.float()                                        # rotary frequencies
+        ang = torch.arange(max_positions, device=self.dev, dtype=torch.float64)[:, None] * inv[None, :]
+        self._cos = torch.cos(ang).float().contiguous()                # [positions, dh / 2]
+        self._sin = torch.sin(ang).float().contiguous()
         self.max_positions = max_positions
+
+    @classmethod
+    def from_weights(cls, hf_cfg, W, device="cuda", fmt="int4", max_positions=None):
+        """The decoder of a Llama-family checkpoint: ``hf_cfg`` its config.json as a dict, ``W`` its weights by
+        Hugging Face name ([out, in] arrays or tensors), read as the reference's ``hub_models.Decoder`` reads
+        them (apsi/hub_models.py:537-563; q/k/v and gate/up fused as its ``_groups``, :572-585).  The
+        projections are quantised to ``fmt`` by this library's kernels; norms and embeddings are kept in
+        bfloat16.  Variants the kernels here do not cover (Gemma's norm offset, q/k norms, projection biases,
+        partial rotary, rope scaling, sliding windows, GPT-2) are refused."""
+        import numpy as np
+        c = dict(hf_cfg)
+        t = c.get("model_type", "llama")
+        unsupported = [k for k in ("rope_scaling", "sliding_window", "partial_rotary_factor") if c.get(k)]
+        if t.startswith("gemma") or t == "gpt2" or unsupported:
+            raise LowbitError(LB_E_ARG, f"decoder variant not covered: model_type {t} {unsupported}")
+        if any(k.endswith(("q_norm.weight", "k_norm.weight", "_proj.bias")) for k in W):
+            raise LowbitError(LB_E_ARG, "q/k norms and projection biases are not covered")
+        H = int(c["hidden_size"])
+        nh = int(c["num_attention_heads"])
+        kvh = int(c.get("num_key_value_heads") or nh)
+        dh = int(c.get("head_dim") or H // nh)
+        emb = W["model.embed_tokens.weight"]
+        cfg = DecoderConfig(H=H, L=int(c["num_hidden_layers"]), nh=nh, kvh=kvh, dh=dh,
+                            I=int(c["intermediate_size"]), V=int(emb.shape[0]), eps=float(c.get("rms_norm_eps", 1e-6)),
+                            theta=float(c.get("rope_theta", 10000.0)))
+        self = cls.__new__(cls)
+        self._setup(cfg, device, fmt, max_positions or int(c.get("max_position_embeddings", 4096)))
+
+        def dev32(a):
+            return torch.as_tensor(np.asarray(a, np.float32) if not isinstance(a, torch.Tensor) else a,
+                                   dtype=torch.float32).to(self.dev).contiguous()
+
+        def proj(*names):
+            return _Proj(torch.cat([dev32(W[n]) for n in names], 0), self.fmt)
+
+        def vec(n):
+            return dev32(W[n]).to(torch.bfloat16)
+
+        self.embed = dev32(emb).to(torch.bfloat16)
+        self.layers = []
+        for i in range(cfg.L):
+            p = f"model.layers.{i}."
+            self.layers.append({
+                "ln1": vec(p + "input_layernorm.weight"),
+                "qkv": proj(p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight", p + "self_attn.v_proj.weight"),
+                "o": proj(p + "self_attn.o_proj.weight"),
+                "ln2": vec(p + "post_attention_layernorm.weight"),
+                "gu": proj(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"),
+                "down": proj(p + "mlp.down_proj.weight"),
+            })
+        self.norm = vec("model.norm.weight")
+        self.head = proj("lm_head.weight" if "lm_head.weight" in W else "model.embed_tokens.weight")
+        return self
 
     # ------------------------------------------------------------------ pieces
     def weight_bytes(self):
@@ -165,13 +225,16 @@ class QuantDecoder:
         return self.head(X_last.contiguous(), static=X_last.shape[0] <= 16, ln=self.norm, eps=self.cfg.eps)
 
     # ------------------------------------------------------------------ forward passes
-    def prefill(self, ids, cache):
-        """ids [B, T] -> logits [B, V] of the last position; fills cache slots [0, T)."""
+    def prefill(self, ids, cache, all_positions=False):
+        """ids [B, T] -> logits [B, V] of the last position (all_positions: [B, T, V]); fills cache slots
+        [0, T)."""
         B, T = ids.shape
         X = self.embed.index_select(0, ids.reshape(-1)).contiguous()   # [B*T, H]
         pos = torch.arange(T, device=self.dev)
         for i in range(self.cfg.L):
             self._block(i, X, B, T, cache, pos, 0, None)
+        if all_positions:
+            return self._logits(X).view(B, T, -1)
         return self._logits(X.view(B, T, -1)[:, -1])
 
     def decode_step(self, tok, cache, pos_t):

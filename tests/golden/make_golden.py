@@ -260,7 +260,31 @@ def hub_cpu_q8(path=None):
     print("wrote", path)
 
 
+def decoder_logits(path=None):
+    """Golden logits of the reference's decoder (``apsi.hub_models.Decoder.forward`` on its processor path,
+    apsi/hub_models.py:1150-1200, the layer sequence its GPU path runs too) on the int4-g128-exact weights of
+    tiny_decoder.py: the logits of a prompt, then of four tokens fed one at a time through the cache, in
+    decoder_golden.npz with a checksum of the weights."""
+    from apsi import hub_models  # noqa: E402  (after _reference() put the reference on the path)
+    sys.path.insert(0, HERE)
+    import tiny_decoder as TD
+    W = TD.weights()
+    dec = hub_models.Decoder(dict(TD.CFG), W)
+    ids = TD.token_ids()
+    cache = dec.new_cache()
+    out = {"ids": ids, "checksum": np.float64(TD.checksum(W)),
+           "prompt_logits": np.asarray(dec.forward(np.array([ids[:TD.PROMPT]]), cache, 0)[0], np.float32)}
+    steps = []
+    for j in range(TD.PROMPT, TD.PROMPT + TD.DECODE):
+        steps.append(np.asarray(dec.forward(np.array([[ids[j]]]), cache, j, last=True)[0, -1], np.float32))
+    out["decode_logits"] = np.stack(steps)
+    path = path or os.path.join(HERE, "decoder_golden.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path)
+
+
 if __name__ == "__main__":
     main()
     precision_api(_reference()[0])
     hub_cpu_q8()
+    decoder_logits()
