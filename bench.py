@@ -150,19 +150,31 @@ def _q8_layer(M, seed=0):
     return codes, scales, x
 
 
+Q8_COPIES = 6          # distinct Q8_0 copies of the layer (6 x 50.7 MB): products stream from DRAM, not the L3
+
+
+def _q8_layers(M):
+    """Q8_COPIES distinct copies of configs[1]'s layer in Q8_0 (a decode step reads each layer once, so the
+    CPU product must not be served from the host's last-level cache) and M tokens."""
+    layers = [_q8_layer(M, seed=s)[:2] for s in range(Q8_COPIES)]
+    return layers, _q8_layer(M)[2]
+
+
 def time_hub_q8(M, reps, warmup=2, threads=0):
     """The reference's fastest CPU product (hub_cpu.matmul on Q8_0 weights, all cores), restated in
-    oracle/hub_q8.c, on configs[1]'s [11008, 4096] layer at M tokens: seconds per product (median of `reps`)."""
+    oracle/hub_q8.c, on configs[1]'s [11008, 4096] layer at M tokens, rotating over Q8_COPIES copies: seconds
+    per product (median of `reps`)."""
     from oracle import hub_q8
-    codes, scales, x = _q8_layer(M)
-    for _ in range(warmup):
-        hub_q8.matmul(x, codes, scales, threads)
+    layers, x = _q8_layers(M)
+    for i in range(warmup):
+        hub_q8.matmul(x, *layers[i % Q8_COPIES], threads)
     ts = []
-    for _ in range(reps):
+    for i in range(reps):
+        c, s_ = layers[i % Q8_COPIES]
         t0 = time.perf_counter()
-        hub_q8.matmul(x, codes, scales, threads)
+        hub_q8.matmul(x, c, s_, threads)
         ts.append(time.perf_counter() - t0)
-    return float(np.median(ts)), codes.nbytes + scales.nbytes
+    return float(np.median(ts)), layers[0][0].nbytes + layers[0][1].nbytes
 
 
 def cpu_baseline_sample():
@@ -182,9 +194,10 @@ def cpu_baseline_sample():
     O.qmatmul_dequant_reference(x, packed, s16, "int4_g128")
     dn = time.perf_counter() - t0
     return {"value": round(weight_bytes(N1, K1) / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"200 products of configs[1]'s [11008,4096] layer at M=1 through oracle/hub_q8.c, the C "
-                      f"restatement of hub_cpu.matmul on Q8_0 weights (the reference's fastest CPU path; its "
-                      f"thread team over {threads} threads): {dt * 1e3:.3f} ms per product, "
+            "sample": f"200 products of configs[1]'s [11008,4096] layer at M=1, rotating over {Q8_COPIES} distinct "
+                      f"Q8_0 copies (weights from DRAM), through oracle/hub_q8.c, the C restatement of "
+                      f"hub_cpu.matmul on Q8_0 weights (the reference's fastest CPU path; its thread team over "
+                      f"{threads} threads): {dt * 1e3:.3f} ms per product, "
                       f"{q8_bytes / dt / 1e9:.1f} GB/s of Q8_0 bytes; value = int4-g128 bytes of the same layer "
                       f"per second",
             "numpy_qmatmul": {"ms_per_product": round(dn * 1e3, 1),
@@ -202,24 +215,26 @@ def run_reference(args, rank):
         return 0
     from oracle import hub_q8
     threads = hub_q8.host_threads()
-    codes, scales, x = _q8_layer(M1)
-    for _ in range(max(args.warmup, 1)):
-        hub_q8.matmul(x, codes, scales, threads)
+    layers, x = _q8_layers(M1)
+    for i in range(max(args.warmup, 1)):
+        hub_q8.matmul(x, *layers[i % Q8_COPIES], threads)
     ts = []
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        c, s_ = layers[i % Q8_COPIES]
         t0 = time.perf_counter()
-        hub_q8.matmul(x, codes, scales, threads)
+        hub_q8.matmul(x, c, s_, threads)
         ts.append(time.perf_counter() - t0)
     dt = float(np.sum(ts)) / args.steps
     val = weight_bytes(N1, K1) / dt / 1e9
-    q8b = codes.nbytes + scales.nbytes
+    q8b = layers[0][0].nbytes + layers[0][1].nbytes
     per_m = {}
     for M in (4, 16):
         dm, _ = time_hub_q8(M, reps=max(5, args.steps // 4), threads=threads)
         per_m[f"M={M}"] = {"ms_per_product": round(dm * 1e3, 4), "value": round(weight_bytes(N1, K1) / dm / 1e9, 3),
                            "q8_weight_GB_per_s": round(q8b / dm / 1e9, 2)}
-    sample = (f"one product of configs[1]'s [11008,4096] layer per step at M=1 through oracle/hub_q8.c, the C "
-              f"restatement of hub_cpu.matmul on Q8_0 weights with its thread team over {threads} threads")
+    sample = (f"one product of configs[1]'s [11008,4096] layer per step at M=1 (rotating over {Q8_COPIES} distinct "
+              f"Q8_0 copies, so the weights come from DRAM) through oracle/hub_q8.c, the C restatement of "
+              f"hub_cpu.matmul on Q8_0 weights with its thread team over {threads} threads")
     out = {"impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32->f32", "data": "synthetic",
