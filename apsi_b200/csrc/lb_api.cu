@@ -302,7 +302,7 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_workspace_size: sizes must be positive");
   if (!use_gemv(M) && is_fp6(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 formats have a product for M <= 16 only");
-  *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
+  *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, N, K);
   return LB_OK;
 }
 
@@ -327,7 +327,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void*
   if (use_gemv(M) && K > gemv_max_k(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: K (%lld) above %d is not supported for M <= 16", (long long)K,
                 gemv_max_k(fmt));
-  size_t need = use_gemv(M) ? 0 : gemm_workspace_bytes(M, K);
+  size_t need = use_gemv(M) ? 0 : gemm_workspace_bytes(M, N, K);
   if (need) {
     if (!workspace || ws_bytes < need)
       return fail(LB_E_WORKSPACE, "lb_linear: workspace of %zu bytes needed (got %zu)", need, workspace ? ws_bytes : 0);

@@ -14,11 +14,21 @@
 // factor so the conversion is exact (bf16 mantissas fit in fp16) and cannot overflow; the factor is undone in
 // the epilogue.  int8 rows keep exact codes and apply the row scale in float32 in the epilogue.
 //
-// Roles (14 warps, persistent over tiles):
+// Roles (14 warps, persistent over work units):
 //   warp 0        TMA producer: activation tile (BN x 64 fp16, SW128) + raw code tile (128 rows) per stage
 //   warp 1        TMEM allocator and MMA issuer (one thread): 4 x tcgen05.mma K=16 per stage, commit -> mbarrier
 //   warps 2..9    dequantise one row x one half of the stage's K into the A tile (st.shared + proxy fence)
 //   warps 10..13  epilogue: tcgen05.ld -> scale / bias / accumulate -> bf16 -> global
+// Measured and not kept for narrow token tiles ([28672, 8192] at M = 64, 121 us as built): a separate code ring
+// up to 32 k-steps deep beside 4 x / A stages (131 us), and 128-byte-wide code tiles (4 k-steps of a row per
+// copy, SWIZZLE_128B, 16 k-steps in flight) beside 6 x / A stages (125 us).  With the dequantisation, the
+// MMAs and the activation reloads all removed the same pipeline still took 66 us: the stage round trip, not
+// the code stream, sets the pace there.
+//
+// Split K (M <= 128 and long K): a tile's k-steps are cut into `splits` equal parts computed by different CTAs;
+// each writes its float32 accumulators to a workspace and splitk_reduce_kernel adds the parts in split order
+// and applies the epilogue.  The split count depends on M and K only, so column shards sum the same way.
+//
 // All mbarrier waits are bounded (lb::mbar_wait); a timeout sets the device error word and the CTA drains.
 #include <string.h>
 #include "lb_common.cuh"
@@ -36,14 +46,23 @@ constexpr int THREADS = (2 + DQ_WARPS + EPI_WARPS) * 32;   // TMA, MMA, dequanti
 constexpr int A_STAGE = BM * BK * 2;                       // 16 KB of fp16 weights per stage
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int TAIL = 512;                                  // mbarriers, TMEM address, abort flag
+__host__ __device__ constexpr int raw_bytes(int fmt) { return BM * ((fmt == 2 || fmt == 9) ? 32 : 64); }
 // Pipeline depth: as many stages as shared memory holds (at most 8).  Narrow token tiles (small M) carry few
 // weight bytes per stage, so they need the deepest pipelines to keep enough of the weight stream in flight.
 __host__ __device__ constexpr int stages(int fmt, int bn) {
-  const int stage = bn * 128 + A_STAGE + BM * ((fmt == 2 || fmt == 9) ? 32 : 64);
-  const int n = (SMEM_LIMIT - 1024 - TAIL) / stage;
-  return n > 8 ? 8 : n;
+  return (SMEM_LIMIT - 1024 - TAIL) / (bn * 128 + A_STAGE + raw_bytes(fmt)) > 8
+             ? 8 : (SMEM_LIMIT - 1024 - TAIL) / (bn * 128 + A_STAGE + raw_bytes(fmt));
 }
 }  // namespace gemm
+
+// K splits (see the file comment): M <= 128 and at least 224 k-steps, about 112 k-steps per split, at most 8;
+// the k-steps of a split are even (a whole number of int4 scale groups).
+// Depends on M and K only.
+__host__ __device__ inline int gemm_splits(int64_t M, int64_t K) {
+  if (M > 128) return 1;
+  const int64_t s = (K / gemm::BK) / 112;
+  return s < 2 ? 1 : (s > 8 ? 8 : static_cast<int>(s));
+}
 
 struct GemmParams {
   const __half* s16;        // int4: [N, K/128]; int8: [N]
@@ -57,11 +76,21 @@ struct GemmParams {
   // idle, tiles full .. tiles - 1 are each cut along the tokens into `parts` units of sbn = BN / parts tokens
   // (the MMA's N and the activation box shrink; k order and accumulation per output are unchanged).
   int units, full, parts, sbn;
+  int splits, kper;         // K splits (1: none) and k-steps per split (even)
+  float* part;              // splits > 1: float32 accumulators [splits][M][N]
   OutRanks dst;             // column-sharded layer: every rank's output (dst.n == 0: y)
 };
 
-// unit -> weight row block, first token, tokens
-__device__ __forceinline__ void gemm_unit(const GemmParams& p, int u, int bn, int& mb, int& tok0, int& width) {
+// unit -> weight row block, first token, tokens, k-steps [k0, k1), split
+__device__ __forceinline__ void gemm_unit(const GemmParams& p, int u, int bn, int& mb, int& tok0, int& width, int& k0,
+                                          int& k1, int& split) {
+  split = 0;
+  if (p.splits > 1) {
+    split = u % p.splits;
+    u /= p.splits;
+  }
+  k0 = split * p.kper;
+  k1 = k0 + p.kper < p.ksteps ? k0 + p.kper : p.ksteps;
   int tile, part = 0;
   if (u < p.full) {
     tile = u;
@@ -242,6 +271,28 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// Epilogue value of one output: fp32 accumulator * token factor * row scale + bias, then stored (accumulated into
+// y, or into every rank's output for a column-sharded layer).
+template <bool SH>
+__device__ __forceinline__ void gemm_store(const GemmParams& p, int64_t tok, int64_t row, float v) {
+  if constexpr (SH) {                       // this rank's column of every rank's output
+    const uint16_t bb = f32_to_bf16_bits_g(v);
+    const int64_t off = tok * p.ldy + p.dst.col0 + row;
+    for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = bb;
+  } else {
+    uint16_t* yp = p.y + tok * p.ldy + row;
+    if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
+    *yp = f32_to_bf16_bits_g(v);
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ float gemm_row_scale(const GemmParams& p, int64_t rowc) {
+  if (FMT == 1) return __half2float(p.s16[rowc]);
+  if (FMT == 5 || FMT == 6 || FMT == 9) return reinterpret_cast<const float*>(p.s16)[rowc];   // float32 row scales
+  return 1.f;
+}
+
 // SH: column-sharded outputs (stores into every rank's buffer); a separate instance, so the ordinary
 // epilogue carries no extra code
 template <int FMT, int BN, bool SH>
@@ -259,10 +310,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   uint8_t* as = xs + STAGES * Sm::X_STAGE;                     // STAGES x A_STAGE  (dequantisers, SW128)
   uint8_t* raw = as + STAGES * A_STAGE;                        // STAGES x RAW_STAGE (TMA)
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + STAGES * Cfg::RAW_STAGE);
-  uint64_t* full_x = bars;
-  uint64_t* full_w = bars + STAGES;
-  uint64_t* a_full = bars + 2 * STAGES;
-  uint64_t* empty = bars + 3 * STAGES;
+  uint64_t* full_x = bars;                                     // activation tile landed
+  uint64_t* full_w = bars + STAGES;                            // code tile landed
+  uint64_t* a_full = bars + 2 * STAGES;                        // A tile written
+  uint64_t* empty = bars + 3 * STAGES;                         // MMAs done with the slot
   uint64_t* acc_full = bars + 4 * STAGES;                      // [2]
   uint64_t* acc_empty = acc_full + 2;                          // [2]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
@@ -303,9 +354,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-        int mb, tok0, width;
-        gemm_unit(p, u, BN, mb, tok0, width);
-        for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+        int mb, tok0, width, k0, k1, sp;
+        gemm_unit(p, u, BN, mb, tok0, width, k0, k1, sp);
+        for (int ks = k0; ks < k1; ++ks, ++it) {
           const uint32_t slot = it % STAGES;
           if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
           mbar_arrive_expect_tx(&full_x[slot], static_cast<uint32_t>(width) * 128u);
@@ -320,14 +371,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0, tcount = 0;
       for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tcount) {
-        int mb, tok0, width;
-        gemm_unit(p, u, BN, mb, tok0, width);
+        int mb, tok0, width, k0, k1, sp;
+        gemm_unit(p, u, BN, mb, tok0, width, k0, k1, sp);
         const uint32_t idesc = idesc_f16_f32(BM, width);
         const uint32_t b = tcount & 1;
         if (tcount >= 2) mbar_wait(&acc_empty[b], ((tcount >> 1) - 1) & 1, abort_v);   // epilogue of tile - 2
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * BN;
-        for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+        for (int ks = k0; ks < k1; ++ks, ++it) {
           const uint32_t slot = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           mbar_wait(&full_x[slot], ph, abort_v);
@@ -338,7 +389,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             tc_mma_ss(d_tmem, smem_desc_sw128(aaddr + kk * 32), smem_desc_sw128(xaddr + kk * 32), idesc,
-                      (ks > 0 || kk > 0) ? 1u : 0u);
+                      (ks > k0 || kk > 0) ? 1u : 0u);
           tc_commit(&empty[slot]);
         }
         tc_commit(&acc_full[b]);
@@ -352,24 +403,25 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const uint32_t arow = static_cast<uint32_t>((rloc >> 3) * 1024 + (rloc & 7) * 128);
     uint32_t it = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-      int mb, tok0, width;
-      gemm_unit(p, u, BN, mb, tok0, width);
+      int mb, tok0, width, k0, k1, sp;
+      gemm_unit(p, u, BN, mb, tok0, width, k0, k1, sp);
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
       // int4 scales of this row, one group of 128 per two stages, fetched four groups ahead through a small
-      // register queue so their latency does not stall a stage
+      // register queue so their latency does not stall a stage (k0 is even: a split starts on a group)
       static_assert(BK * 2 == 128, "two stages per scale group");
       const int ng = static_cast<int>(p.K / 128);
+      const int g0 = k0 >> 1;
       const unsigned short* srow = reinterpret_cast<const unsigned short*>(p.s16) + rowc * ng;
       unsigned short sq0 = 0, sq1 = 0, sq2 = 0, sq3 = 0;
       if (FMT == 2) {
-        sq0 = __ldg(srow);
-        if (ng > 1) sq1 = __ldg(srow + 1);
-        if (ng > 2) sq2 = __ldg(srow + 2);
-        if (ng > 3) sq3 = __ldg(srow + 3);
+        sq0 = __ldg(srow + g0);
+        if (g0 + 1 < ng) sq1 = __ldg(srow + g0 + 1);
+        if (g0 + 2 < ng) sq2 = __ldg(srow + g0 + 2);
+        if (g0 + 3 < ng) sq3 = __ldg(srow + g0 + 3);
       }
       uint32_t s2 = 0;
-      for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+      for (int ks = k0; ks < k1; ++ks, ++it) {
         const uint32_t slot = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         if (FMT == 2 && (ks & 1) == 0) {
@@ -416,38 +468,40 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     uint32_t tcount = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tcount) {
-      int mb, tok0, width;
-      gemm_unit(p, u, BN, mb, tok0, width);
+      int mb, tok0, width, k0, k1, sp;
+      gemm_unit(p, u, BN, mb, tok0, width, k0, k1, sp);
       const int64_t row = static_cast<int64_t>(mb) * BM + rloc;
       const int64_t rowc = row < p.N ? row : p.N - 1;
       const uint32_t b = tcount & 1;
       mbar_wait(&acc_full[b], (tcount >> 1) & 1, abort_v);
       tc_fence_after();
-      float rs = 1.f, bias = 0.f;
-      if (FMT == 1) rs = __half2float(p.s16[rowc]);
-      if (FMT == 5 || FMT == 6 || FMT == 9) rs = reinterpret_cast<const float*>(p.s16)[rowc];   // fp8 / fp4 rows: float32 scales
-      if (p.bias) bias = __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16);
+      const float rs = gemm_row_scale<FMT>(p, rowc);
+      const float bias = p.bias ? __uint_as_float(static_cast<uint32_t>(p.bias[rowc]) << 16) : 0.f;
       const bool row_ok = row < p.N;
+      if (p.splits > 1) {                   // this split's float32 accumulators; the reduction does the rest
+        float* dst = p.part + static_cast<int64_t>(sp) * p.M * p.N + row;
 #pragma unroll 1
-      for (int c0 = 0; c0 < width; c0 += 16) {
-        uint32_t dv[16];
-        tmem_ld_x16(tmem + lane_addr + b * BN + c0, dv);
-        tc_wait_ld();
+        for (int c0 = 0; c0 < width; c0 += 16) {
+          uint32_t dv[16];
+          tmem_ld_x16(tmem + lane_addr + b * BN + c0, dv);
+          tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int64_t tok = static_cast<int64_t>(tok0) + c0 + j;
-          if (row_ok && tok < p.M) {
-            float v = __uint_as_float(dv[j]) * (p.tokscale[tok] * rs);
-            v += bias;
-            if constexpr (SH) {             // this rank's column of every rank's output
-              const uint16_t bb = f32_to_bf16_bits_g(v);
-              const int64_t off = tok * p.ldy + p.dst.col0 + row;
-              for (int g = 0; g < p.dst.n; ++g) p.dst.y[g][off] = bb;
-            } else {
-              uint16_t* yp = p.y + tok * p.ldy + row;
-              if (p.acc) v += __uint_as_float(static_cast<uint32_t>(*yp) << 16);
-              *yp = f32_to_bf16_bits_g(v);
-            }
+          for (int j = 0; j < 16; ++j) {
+            const int64_t tok = static_cast<int64_t>(tok0) + c0 + j;
+            if (row_ok && tok < p.M) dst[tok * p.N] = __uint_as_float(dv[j]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < width; c0 += 16) {
+          uint32_t dv[16];
+          tmem_ld_x16(tmem + lane_addr + b * BN + c0, dv);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int64_t tok = static_cast<int64_t>(tok0) + c0 + j;
+            if (row_ok && tok < p.M)
+              gemm_store<SH>(p, tok, row, __uint_as_float(dv[j]) * (p.tokscale[tok] * rs) + bias);
           }
         }
       }
@@ -465,18 +519,41 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   }
 }
 
+// The K splits of a tile added in split order, then the epilogue of gemm_kernel: one thread per output.
+template <int FMT, bool SH>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmParams p) {
+  const int64_t total = p.M * p.N;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tok = i / p.N, row = i - tok * p.N;
+    float v = p.part[i];
+    for (int s = 1; s < p.splits; ++s) v += p.part[s * total + i];
+    const float rs = gemm_row_scale<FMT>(p, row);
+    const float bias = p.bias ? __uint_as_float(static_cast<uint32_t>(p.bias[row]) << 16) : 0.f;
+    gemm_store<SH>(p, tok, row, v * (p.tokscale[tok] * rs) + bias);
+  }
+}
+
 // ------------------------------------------------------------------------------------------- host side
 static int gemm_bn_for(int64_t M) { return M <= 64 ? 64 : (M <= 128 ? 128 : 256); }
 
 size_t gemm_smem_bytes(int fmt, int bn) {
-  const int raw = (fmt == 2 || fmt == 9) ? GemmCfg<2>::RAW_STAGE : GemmCfg<1>::RAW_STAGE;
-  return 1024 + static_cast<size_t>(gemm::stages(fmt, bn)) * (bn * 128 + gemm::A_STAGE + raw) + gemm::TAIL;
+  return 1024 + static_cast<size_t>(gemm::stages(fmt, bn)) * (bn * 128 + gemm::A_STAGE + gemm::raw_bytes(fmt)) +
+         gemm::TAIL;
 }
 
-size_t gemm_workspace_bytes(int64_t M, int64_t K) {
+// Workspace layout: fp16 activations [M, K] | per-token factors [M] | (K splits) float32 accumulators
+// [splits][M][N], each part 256-byte aligned.
+static size_t ws_front_bytes(int64_t M, int64_t K) {
   size_t x16 = static_cast<size_t>(M * K) * 2;
   x16 = (x16 + 255) & ~static_cast<size_t>(255);
-  return x16 + static_cast<size_t>(M) * sizeof(float) + 256;
+  return x16 + ((static_cast<size_t>(M) * sizeof(float) + 255) & ~static_cast<size_t>(255));
+}
+
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  const int splits = gemm_splits(M, K);
+  const size_t part = splits > 1 ? static_cast<size_t>(splits) * M * N * sizeof(float) : 0;
+  return ws_front_bytes(M, K) + part + 256;
 }
 
 template <int FMT, int BN, bool SH>
@@ -487,14 +564,32 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tw, c
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, BN, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, BN, SH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   const int grid = p.units < sms ? p.units : sms;
   gemm_kernel<FMT, BN, SH><<<grid, gemm::THREADS, smem, st>>>(tx, tw, txs, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int64_t total = p.M * p.N;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
+  splitk_reduce_kernel<FMT, SH><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
   return cudaGetLastError();
+}
+
+// the instance for a format: token tile, sharded outputs
+template <int FMT>
+static cudaError_t launch_gemm_f(int bn, bool sh, const CUtensorMap& tx, const CUtensorMap& tw,
+                                 const CUtensorMap& txs, const GemmParams& p, int sms, cudaStream_t st) {
+  if (bn == 64) return sh ? launch_gemm_t<FMT, 64, true>(tx, tw, txs, p, sms, st)
+                          : launch_gemm_t<FMT, 64, false>(tx, tw, txs, p, sms, st);
+  if (bn == 128) return sh ? launch_gemm_t<FMT, 128, true>(tx, tw, txs, p, sms, st)
+                           : launch_gemm_t<FMT, 128, false>(tx, tw, txs, p, sms, st);
+  return sh ? launch_gemm_t<FMT, 256, true>(tx, tw, txs, p, sms, st)
+            : launch_gemm_t<FMT, 256, false>(tx, tw, txs, p, sms, st);
 }
 
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
@@ -505,11 +600,12 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     *why = "cuTensorMapEncodeTiled is not available from the driver";
     return cudaErrorNotSupported;
   }
-  // workspace: permuted fp16 activations + per-token factors
+  // workspace: permuted fp16 activations + per-token factors (+ K-split accumulators)
   size_t x16b = static_cast<size_t>(M * K) * 2;
   x16b = (x16b + 255) & ~static_cast<size_t>(255);
   uint16_t* x16 = reinterpret_cast<uint16_t*>(ws);
   float* tokscale = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + x16b);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ws_front_bytes(M, K));
   {
     const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
     if (fmt == 2)
@@ -569,7 +665,17 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   p.full = p.tiles;
   p.parts = 1;
   p.sbn = BN;
-  {
+  p.splits = gemm_splits(M, K);
+  p.kper = p.ksteps;
+  p.part = part;
+  if (p.splits > 1) {                 // equal, even k-step counts; no split left empty
+    p.kper = (p.ksteps + p.splits - 1) / p.splits;
+    p.kper += p.kper & 1;
+    p.splits = (p.ksteps + p.kper - 1) / p.kper;
+  }
+  if (p.splits > 1) {
+    p.units = p.tiles * p.splits;
+  } else {
     const int rem = p.tiles % sms;
     if (BN >= 128 && p.tiles > sms && rem > 0 && rem * 2 <= sms) {
       int parts = BN / 64;
@@ -597,50 +703,13 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     }
   }
   p.dst = dst ? *dst : OutRanks{};
-  if (fmt == 2) {
-    if (p.dst.n) {
-      if (BN == 64) return launch_gemm_t<2, 64, true>(tx, tw, txs, p, sms, st);
-      if (BN == 128) return launch_gemm_t<2, 128, true>(tx, tw, txs, p, sms, st);
-      return launch_gemm_t<2, 256, true>(tx, tw, txs, p, sms, st);
-    }
-    if (BN == 64) return launch_gemm_t<2, 64, false>(tx, tw, txs, p, sms, st);
-    if (BN == 128) return launch_gemm_t<2, 128, false>(tx, tw, txs, p, sms, st);
-    return launch_gemm_t<2, 256, false>(tx, tw, txs, p, sms, st);
+  switch (fmt) {
+    case 2: return launch_gemm_f<2>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    case 9: return launch_gemm_f<9>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    case 5: return launch_gemm_f<5>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    case 6: return launch_gemm_f<6>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    default: return launch_gemm_f<1>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
   }
-  if (fmt == 9) {
-    if (p.dst.n) {
-      if (BN == 64) return launch_gemm_t<9, 64, true>(tx, tw, txs, p, sms, st);
-      if (BN == 128) return launch_gemm_t<9, 128, true>(tx, tw, txs, p, sms, st);
-      return launch_gemm_t<9, 256, true>(tx, tw, txs, p, sms, st);
-    }
-    if (BN == 64) return launch_gemm_t<9, 64, false>(tx, tw, txs, p, sms, st);
-    if (BN == 128) return launch_gemm_t<9, 128, false>(tx, tw, txs, p, sms, st);
-    return launch_gemm_t<9, 256, false>(tx, tw, txs, p, sms, st);
-  }
-  if (fmt == 5 || fmt == 6) {
-    if (p.dst.n) {
-      if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, true>(tx, tw, txs, p, sms, st)
-                                    : (BN == 128 ? launch_gemm_t<5, 128, true>(tx, tw, txs, p, sms, st)
-                                                 : launch_gemm_t<5, 256, true>(tx, tw, txs, p, sms, st));
-      return BN == 64 ? launch_gemm_t<6, 64, true>(tx, tw, txs, p, sms, st)
-                      : (BN == 128 ? launch_gemm_t<6, 128, true>(tx, tw, txs, p, sms, st)
-                                   : launch_gemm_t<6, 256, true>(tx, tw, txs, p, sms, st));
-    }
-    if (fmt == 5) return BN == 64 ? launch_gemm_t<5, 64, false>(tx, tw, txs, p, sms, st)
-                                  : (BN == 128 ? launch_gemm_t<5, 128, false>(tx, tw, txs, p, sms, st)
-                                               : launch_gemm_t<5, 256, false>(tx, tw, txs, p, sms, st));
-    return BN == 64 ? launch_gemm_t<6, 64, false>(tx, tw, txs, p, sms, st)
-                    : (BN == 128 ? launch_gemm_t<6, 128, false>(tx, tw, txs, p, sms, st)
-                                 : launch_gemm_t<6, 256, false>(tx, tw, txs, p, sms, st));
-  }
-  if (p.dst.n) {
-    if (BN == 64) return launch_gemm_t<1, 64, true>(tx, tw, txs, p, sms, st);
-    if (BN == 128) return launch_gemm_t<1, 128, true>(tx, tw, txs, p, sms, st);
-    return launch_gemm_t<1, 256, true>(tx, tw, txs, p, sms, st);
-  }
-  if (BN == 64) return launch_gemm_t<1, 64, false>(tx, tw, txs, p, sms, st);
-  if (BN == 128) return launch_gemm_t<1, 128, false>(tx, tw, txs, p, sms, st);
-  return launch_gemm_t<1, 256, false>(tx, tw, txs, p, sms, st);
 }
 
 }  // namespace lb

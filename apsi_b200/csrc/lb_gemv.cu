@@ -84,6 +84,7 @@ struct GemvParams {
   int ln_f32, ln_vec;     // weights are float32; weights are 16-byte aligned
   float ln_eps, ln_off;
   int scale_tma;          // box mode: the item's scales come with it (tensor map `ts`)
+  int pre;                // integer path: weight copies issued before the activations' loads are (all queued)
 };
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
@@ -312,7 +313,7 @@ __host__ __device__ inline GemvSmem gemv_smem(int fmt, int M, int MT, int G, int
   s.ptab = s.gred + G * 2 * GW * 32 * (fmt == 20 ? 2 : 4) * MT * 4;   // double-buffered group partials
   s.zeros = s.ptab + ((items * 16 * M * 4 + 127) & ~127);
   s.bars = s.zeros + 256;                                      // 256 zero bytes (absent tokens)
-  s.lnf = s.bars + 2 * MAX_SLOTS * 8 + 16;                    // [16] RMSNorm factors per token
+  s.lnf = s.bars + 2 * MAX_SLOTS * 8 + 32;                    // [16] RMSNorm factors per token
   s.total = s.lnf + 64;
   return s;
 }
@@ -382,6 +383,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(dyn_smem + L.bars);
   uint64_t* empty_bar = full_bar + MAX_SLOTS;
   volatile int* abort_v = reinterpret_cast<int*>(empty_bar + MAX_SLOTS);
+  uint64_t* x_bar = empty_bar + MAX_SLOTS + 2;                 // every consumer warp has issued its x loads
   const int units_staged = nloc * RANGE_UNITS;
   const int slots = p.slots;   // a multiple of G: group g owns slots g, g + G, ...
   // Item q belongs to group q % G and uses that group's slots in turn, so every slot is used by one group, in
@@ -395,6 +397,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < slots; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], GW); }
+    mbar_init(x_bar, NCW);
     *abort_v = 0;
     fence_barrier_init();
   }
@@ -414,6 +417,9 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
       if (p.scale_tma) prefetch_tmap(&ts);
     }
     for (int q = 0; q < nq && !*abort_v; ++q) {
+      // the integer path's activations are loaded after griddepcontrol.wait; copies issued before those
+      // loads would be served first, so past the first `pre` items the stream waits until they are queued
+      if (FMT == 20 && q == p.pre) mbar_wait(x_bar, 0, abort_v);
       const int k = q / nloc, i = q - k * nloc;
       const int64_t row0 = static_cast<int64_t>(cid + k * p.C) * RB;
       const int rows_valid = static_cast<int>(p.N - row0 < RB ? p.N - row0 : RB);
@@ -534,6 +540,7 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
         constexpr int SB = 2;                                             // passes with loads in flight together
         const int npair = p.M * units_staged;
         const int j = lane & 15;
+        if (2 * warp >= npair && lane == 0) mbar_arrive(x_bar);        // no pair for this warp
         for (int base = 2 * warp; base < npair; base += PPI * SB) {      // warp-uniform
           uint4 v[SB];
           RmsW wv[SB];
@@ -554,6 +561,10 @@ __global__ void __launch_bounds__((G * gemv::GW + 1) * 32, MINB)
               v[b] = ldg_nc_v4(p.x + static_cast<int64_t>(t) * p.K + k0);
               if (p.ln) wv[b] = rms_load_w(p.ln, p.ln_f32 != 0, k0, p.K, p.ln_vec != 0);
             }
+          }
+          if (base == 2 * warp) {                // this warp's first loads are issued
+            __syncwarp();
+            if (lane == 0) mbar_arrive(x_bar);
           }
           if (p.ln) {                            // norm prologue: bf16((x * fac) * (w + off)), as lb_rmsnorm
 #pragma unroll
@@ -1176,6 +1187,7 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
   p.ln_eps = ln ? ln->eps : 0.f;
   p.ln_off = ln ? ln->off : 0.f;
   p.scale_tma = 0;
+  p.pre = 1 << 30;
   if (fmt == 7 || fmt == 8) {
     if (ln) return cudaErrorNotSupported;     // the norm prologue lives in gemv_kernel's staging
     const int64_t want = (N + 7) / 8;         // one warp per row
@@ -1208,8 +1220,10 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
         // whole share of the weights at once, with the codes read from the slot unit by unit
         // ([11008, 4096]: 7.15 -> 6.68 us, [28672, 8192]: 25.1 -> 23.4 us); otherwise three slots
         // ([4096, 11008]: 10.2 against 11.0 us, [8192, 28672]: 31.7 against 49 us with six)
-        if (p.nr <= 2 && p.nblocks >= sms)
+        if (p.nr <= 2 && p.nblocks >= sms) {
+          p.pre = 1;   // then the activations' loads, then the rest ([11008, 4096]: 6.65 -> 6.45 us)
           return launch_gemv_t<20, 1, 3, 1, true, true>(p, sms, 1, 6, pdl, st, &tw, &ts);
+        }
         return launch_gemv_t<20, 1, 3, 1, true>(p, sms, 1, 3, pdl, st, &tw, &ts);
       }
     }

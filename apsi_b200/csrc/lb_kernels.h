@@ -39,7 +39,7 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
                         cudaStream_t st, const OutRanks* dst = nullptr, const RmsPrologue* ln = nullptr);
 
-size_t gemm_workspace_bytes(int64_t M, int64_t K);
+size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, void* ws, int sms,
                         cudaStream_t st, const char** why, const OutRanks* dst = nullptr);

@@ -97,7 +97,7 @@ extern "C" int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, c
   if (M > (1LL << 31) || K > (1LL << 31)) return fail(LB_E_ARG, "lb_linear_noalloc: M and K must be below 2^31");
   if (M <= 16)   // decode path: no scratch at all
     return lb_linear_ex(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, nullptr, 0, 0u, stream);
-  const size_t need = gemm_workspace_bytes(M, K);
+  const size_t need = gemm_workspace_bytes(M, N, K);
   if (need > static_cast<size_t>(LB_NOALLOC_SCRATCH_BYTES))
     return fail(LB_E_WORKSPACE,
                 "lb_linear_noalloc: M=%lld, K=%lld needs %zu bytes of scratch, above the fixed %d "

@@ -82,6 +82,10 @@ class QTensor:
     the logical array is ``[in, out]`` and the rows stored are its transpose, see ``quantize_linear``)."""
     __slots__ = ("codes", "scale", "fmt", "shape", "axis", "dim", "packed", "scale16", "group", "kn", "_dev",
                  "_fast")
+    # NumPy defers ``x @ q`` (and every other binary operator) to this class, so a model written with plain
+    # ``x @ p.W`` -- the reference's Linear.apply (apsi/layers.py:251-253), its attention and SwiGLU blocks --
+    # multiplies a QTensor weight through __rmatmul__ and the fused kernels, unchanged
+    __array_ufunc__ = None
 
     def __init__(self, codes, scale, fmt, shape, axis, dim=None, packed=False, scale16=None, group=None, kn=False):
         self.codes, self.scale, self.fmt, self.shape = codes, scale, fmt, tuple(shape)

@@ -283,8 +283,57 @@ def decoder_logits(path=None):
     print("wrote", path)
 
 
+def layers_trace(path=None):
+    """The reference's transformer_lm forward (apsi/layers.py:1999-2008; Linear.apply and the attention / SwiGLU
+    blocks all multiply as ``x @ W``) with every projection weight replaced by its int4-g128 dequantisation
+    (the oracle's quantisation of W.T: rows = outputs, groups of 128 along the inputs).  Each weight is wrapped
+    so that the forward's own ``x @ W`` expressions defer to it (``__array_ufunc__ = None``, the hook this
+    library's QTensor uses); every call's input and output is recorded, in call order, with the packed codes and
+    fp16 scales of its weight and the final logits, in layers_trace_golden.npz."""
+    from apsi import layers as Ly  # noqa: E402  (after _reference() put the reference on the path)
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    import oracle as O
+    model = Ly.transformer_lm(256, d=128, heads=4, layers=1, context=16, rope=True, norm="rms", ffn="swiglu",
+                              ff=256)
+    params = model.init(0)
+    calls = []
+
+    class Traced:
+        __array_ufunc__ = None
+
+        def __init__(self, W, name):
+            packed, _, s16 = O.quant_int4_g128(np.ascontiguousarray(np.asarray(W, np.float32).T))
+            self.name, self.packed, self.s16 = name, packed, s16
+            self.Wd = O.dequant_int4_g128(packed, s16).T.astype(np.float64)      # [in, out]
+            self.shape, self.ndim = self.Wd.shape, 2
+
+        def __rmatmul__(self, x):
+            y = np.asarray(x) @ self.Wd
+            calls.append((self.name, np.asarray(x, np.float32), np.asarray(y, np.float32)))
+            return y
+
+    out = {}
+    blk = params[1][0]
+    targets = [(blk.attn.inner.fields, k) for k in ("Wq", "Wk", "Wv", "Wo")] + \
+              [(blk.mlp.inner.fields, k) for k in ("Wg", "Wu", "Wd")] + [(params[2].fields, "W")]
+    for f, k in targets:
+        t = Traced(f[k], "head" if k == "W" else k)
+        f[k] = t
+        out[f"w_{t.name}_packed"], out[f"w_{t.name}_s16"] = t.packed, t.s16.view(np.uint16)
+    ids = np.random.default_rng(5).integers(0, 256, size=(2, 8))
+    out["ids"] = ids
+    out["logits"] = np.asarray(model(params, ids, train=False), np.float32)
+    out["call_names"] = np.array([c[0] for c in calls])
+    for i, (_, x, y) in enumerate(calls):
+        out[f"call{i}_x"], out[f"call{i}_y"] = x, y
+    path = path or os.path.join(HERE, "layers_trace_golden.npz")
+    np.savez_compressed(path, **out)
+    print("wrote", path, len(calls), "calls")
+
+
 if __name__ == "__main__":
     main()
     precision_api(_reference()[0])
     hub_cpu_q8()
     decoder_logits()
+    layers_trace()

@@ -55,6 +55,7 @@ SHAPES = [
     (8, 2400, 2048), (13, 3000, 6144), (6, 1000, 11008), (8, 4096, 11008),
     (17, 300, 1024), (40, 520, 2048), (64, 1000, 4096), (130, 257, 512), (256, 1024, 1024),  # GEMM
     (300, 520, 2048), (2048, 12288, 4096),                      # configs[2]
+    (64, 1000, 16384), (100, 520, 28672), (128, 384, 14336), (17, 256, 20480),   # K split over CTAs (M <= 128)
 ]
 
 
@@ -80,7 +81,7 @@ def test_bias_and_accumulate(cuda, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(1, 11008, 4096), (4, 4096, 11008), (1, 8192, 28672), (16, 2048, 4096),
                                    (2, 1376, 4096), (1, 28672, 8192), (8, 4096, 11008), (300, 12288, 1024),
-                                   (2048, 12288, 4096)])
+                                   (2048, 12288, 4096), (64, 8192, 28672), (100, 2048, 16384)])
 @pytest.mark.parametrize("shards", [2, 8])
 def test_column_shards_are_bit_identical(cuda, M, N, K, shards):
     """Each shard of rows computed alone (the multi-GPU layout) gives exactly the full product's columns,
