@@ -289,7 +289,7 @@ int lb_gguf_decode(int kind, const uint8_t* blocks, int64_t n, float* out, void*
 static bool use_gemv(int64_t M) { return M <= 16; }
 
 // formats with a fused product: int8 rows, int4 groups of 128, fp8 e4m3 / e5m2, fp6 e3m2 / e2m3 and fp4 e2m1
-// rows (float32 row scales); fp6 has the decode product only (M <= 16)
+// rows (float32 row scales); fp6 rows need K % 16 == 0 for the decode product and K % 64 == 0 above M = 16
 static bool has_product(int fmt) {
   return fmt == LB_FMT_INT8_ROW || fmt == LB_FMT_INT4_G128 || (fmt >= LB_FMT_FP8_E4M3 && fmt <= LB_FMT_FP4_E2M1);
 }
@@ -300,8 +300,8 @@ int lb_linear_workspace_size(int fmt, int64_t M, int64_t N, int64_t K, size_t* b
   if (!has_product(fmt))
     return fail(LB_E_UNSUPPORTED, "lb_linear: format %d has no product kernel in this build", fmt);
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_workspace_size: sizes must be positive");
-  if (!use_gemv(M) && is_fp6(fmt))
-    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 formats have a product for M <= 16 only");
+  if (!use_gemv(M) && is_fp6(fmt) && K % 64)
+    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 products above M = 16 need K %% 64 == 0");
   *bytes = use_gemv(M) ? 0 : gemm_workspace_bytes(M, N, K);
   return LB_OK;
 }
@@ -318,8 +318,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const void*
   if (M > (1LL << 31) || N > (1LL << 31)) return fail(LB_E_ARG, "lb_linear: M and N must be below 2^31");
   const int64_t kmult = (fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP4_E2M1) ? 128 : (is_fp6(fmt) ? 16 : 64);
   if (K % kmult) return fail(LB_E_ARG, "lb_linear: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
-  if (!use_gemv(M) && is_fp6(fmt))
-    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 formats have a product for M <= 16 only");
+  if (!use_gemv(M) && is_fp6(fmt) && K % 64)
+    return fail(LB_E_UNSUPPORTED, "lb_linear: fp6 products above M = 16 need K %% 64 == 0");
   if (ldy < N) return fail(LB_E_ARG, "lb_linear: ldy (%lld) < N (%lld)", (long long)ldy, (long long)N);
   if (!aligned(x, 16) || !aligned(codes, 16) || !aligned(scales, 16))
     return fail(LB_E_ALIGN, "lb_linear: x, codes and scales must be 16-byte aligned");

@@ -46,7 +46,9 @@ constexpr int THREADS = (2 + DQ_WARPS + EPI_WARPS) * 32;   // TMA, MMA, dequanti
 constexpr int A_STAGE = BM * BK * 2;                       // 16 KB of fp16 weights per stage
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int TAIL = 512;                                  // mbarriers, TMEM address, abort flag
-__host__ __device__ constexpr int raw_bytes(int fmt) { return BM * ((fmt == 2 || fmt == 9) ? 32 : 64); }
+// code bytes of a row per k-step: 4-bit 32, 6-bit 48 (four codes per three bytes), 8-bit 64
+__host__ __device__ constexpr int raw_row(int fmt) { return (fmt == 2 || fmt == 9) ? 32 : ((fmt == 7 || fmt == 8) ? 48 : 64); }
+__host__ __device__ constexpr int raw_bytes(int fmt) { return BM * raw_row(fmt); }
 // Pipeline depth: as many stages as shared memory holds (at most 8).  Narrow token tiles (small M) carry few
 // weight bytes per stage, so they need the deepest pipelines to keep enough of the weight stream in flight.
 __host__ __device__ constexpr int stages(int fmt, int bn) {
@@ -107,7 +109,7 @@ __device__ __forceinline__ void gemm_unit(const GemmParams& p, int u, int bn, in
 
 template <int FMT>
 struct GemmCfg {
-  static constexpr int RAW_ROW = (FMT == 2 || FMT == 9) ? 32 : 64;   // code bytes of a row per stage
+  static constexpr int RAW_ROW = gemm::raw_row(FMT);                  // code bytes of a row per stage
   static constexpr int RAW_STAGE = gemm::BM * RAW_ROW;
 };
 
@@ -237,6 +239,32 @@ __device__ __forceinline__ void deq_fp4_f16(const uint4 raw, uint32_t (&o)[16]) 
   }
 }
 
+// fp6 rows: 24 bytes of one row (8 groups of three bytes = 32 codes; value j of a group at bits 6j .. 6j + 5 of
+// its little-endian 24-bit word) -> 16 exact fp16 pairs in natural K order through the hardware conversion;
+// the row scale is applied in the epilogue.
+template <int FMT>
+__device__ __forceinline__ void deq_fp6_f16(const uint32_t (&w)[6], uint32_t (&o)[16]) {
+  const uint32_t g[8] = {w[0] & 0xFFFFFFu, (w[0] >> 24) | ((w[1] << 8) & 0xFFFF00u),
+                         (w[1] >> 16) | ((w[2] << 16) & 0xFF0000u), w[2] >> 8,
+                         w[3] & 0xFFFFFFu, (w[3] >> 24) | ((w[4] << 8) & 0xFFFF00u),
+                         (w[4] >> 16) | ((w[5] << 16) & 0xFF0000u), w[5] >> 8};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    // the four 6-bit fields into the low bits of four bytes, then two codes per conversion
+    const uint32_t u = (g[i] & 0x3Fu) | ((g[i] << 2) & 0x3F00u) | ((g[i] << 4) & 0x3F0000u) | ((g[i] << 6) & 0x3F000000u);
+    uint32_t lo, hi;
+    if (FMT == 7) {
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e3m2x2 %0, a;\n\t}" : "=r"(lo) : "r"(u));
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e3m2x2 %0, a;\n\t}" : "=r"(hi) : "r"(u >> 16));
+    } else {
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e2m3x2 %0, a;\n\t}" : "=r"(lo) : "r"(u));
+      asm("{\n\t.reg .b16 a;\n\tcvt.u16.u32 a, %1;\n\tcvt.rn.f16x2.e2m3x2 %0, a;\n\t}" : "=r"(hi) : "r"(u >> 16));
+    }
+    o[2 * i] = lo;
+    o[2 * i + 1] = hi;
+  }
+}
+
 // fp8 rows: 32 bytes of one row -> 16 fp16 pairs, exact, in the pairing of deq_int8_f16 (bytes (0, 2), (1, 3)
 // of each word): e4m3 through the hardware conversion, e5m2 as the high byte of an fp16.
 template <int FMT>
@@ -289,7 +317,7 @@ __device__ __forceinline__ void gemm_store(const GemmParams& p, int64_t tok, int
 template <int FMT>
 __device__ __forceinline__ float gemm_row_scale(const GemmParams& p, int64_t rowc) {
   if (FMT == 1) return __half2float(p.s16[rowc]);
-  if (FMT == 5 || FMT == 6 || FMT == 9) return reinterpret_cast<const float*>(p.s16)[rowc];   // float32 row scales
+  if (FMT >= 5 && FMT <= 9) return reinterpret_cast<const float*>(p.s16)[rowc];   // fp8 / fp6 / fp4: float32 row scales
   return 1.f;
 }
 
@@ -439,6 +467,17 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           const uint4 r = lds_v4(rbase + 16 * (h ^ ((rloc >> 2) & 1)));
           if (FMT == 2) deq_int4_f16(r, s2, o);
           else deq_fp4_f16(r, o);
+        } else if (FMT == 7 || FMT == 8) {
+          // unswizzled 48-byte rows: this half's 24 bytes as three 8-byte words
+          uint32_t w[6];
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            uint32_t a, b;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(rbase + 24 * h + 8 * j));
+            w[2 * j] = a;
+            w[2 * j + 1] = b;
+          }
+          deq_fp6_f16<FMT>(w, o);
         } else {
           // SWIZZLE_64B: chunk index (0..3) ^= bits 7..8 of the offset (row >> 1)
           const int sw = (rloc >> 1) & 3;
@@ -610,7 +649,7 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
     if (fmt == 2)
       prep_x_kernel<0><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
-    else if (fmt == 9)
+    else if (fmt == 9 || fmt == 7 || fmt == 8)     // codes in natural K order
       prep_x_kernel<2><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
     else
       prep_x_kernel<1><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
@@ -634,15 +673,16 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   }
   {
     const bool nib = (fmt == 2 || fmt == 9);          // 4-bit codes
-    const int64_t row_bytes = nib ? K / 2 : K;
-    const cuuint32_t raw_row = nib ? GemmCfg<2>::RAW_ROW : GemmCfg<1>::RAW_ROW;
+    const bool six = (fmt == 7 || fmt == 8);          // 6-bit codes, four per three bytes
+    const int64_t row_bytes = nib ? K / 2 : (six ? K / 4 * 3 : K);
+    const cuuint32_t raw_row = static_cast<cuuint32_t>(gemm::raw_row(fmt));
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(N)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
     cuuint32_t box[2] = {raw_row, static_cast<cuuint32_t>(gemm::BM)};
     cuuint32_t es[2] = {1, 1};
     CUresult r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(codes), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     nib ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     nib ? CU_TENSOR_MAP_SWIZZLE_32B : (six ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B),
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       *why = "cuTensorMapEncodeTiled failed for the weight codes";
@@ -708,6 +748,8 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
     case 9: return launch_gemm_f<9>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
     case 5: return launch_gemm_f<5>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
     case 6: return launch_gemm_f<6>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    case 7: return launch_gemm_f<7>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
+    case 8: return launch_gemm_f<8>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
     default: return launch_gemm_f<1>(BN, p.dst.n != 0, tx, tw, txs, p, sms, st);
   }
 }

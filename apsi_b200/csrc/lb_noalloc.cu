@@ -90,7 +90,7 @@ extern "C" int lb_linear_noalloc(int fmt, const void* x, int64_t M, int64_t K, c
   using namespace lb;
   const bool fp6 = (fmt == LB_FMT_FP6_E3M2 || fmt == LB_FMT_FP6_E2M3);
   if (fmt != LB_FMT_INT8_ROW && fmt != LB_FMT_INT4_G128 && fmt != LB_FMT_FP8_E4M3 && fmt != LB_FMT_FP8_E5M2 &&
-      fmt != LB_FMT_FP4_E2M1 && !(fp6 && M <= 16))
+      fmt != LB_FMT_FP4_E2M1 && !(fp6 && (M <= 16 || K % 64 == 0)))
     return fail(LB_E_UNSUPPORTED, "lb_linear_noalloc: format %d has no product kernel for M = %lld in this build", fmt,
                 (long long)M);
   if (M <= 0 || N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_linear_noalloc: M, N, K must be positive");

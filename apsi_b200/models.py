@@ -158,7 +158,7 @@ def _pack_for_device(arr, want):
     f = P.get_format(fmt)
     if arr.shape[1] % {4: 128, 6: 16}.get(f.bits, 64):   # rows the fused products take: 4-bit 128k, 6-bit 16k, 8-bit 64k
         return np.asarray(arr, np.float32)
-    w = torch.from_numpy(np.ascontiguousarray(arr, np.float32)).to(torch.device("cuda", torch.cuda.current_device()))
+    w = torch.from_numpy(np.array(arr, np.float32)).to(torch.device("cuda", torch.cuda.current_device()))
     if f.kind == "minifloat":
         return P.quantize(w, fmt, axis=0)
     return P.quantize(w, fmt, axis=0, group=128 if f.bits == 4 else None)

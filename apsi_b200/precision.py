@@ -392,8 +392,8 @@ def qmatmul(a, b, out=None):
 def _minifloat_product(x2, b, R, C, dev, out):
     """x2 [M, C] bfloat16 @ W^T for a minifloat weight W [R, C].  fp8 e4m3 / e5m2: the fused kernels (codes to
     exact fp16, float32 row scales; a tensor scale is broadcast to the rows).  fp4 e2m1 with C % 128 == 0: the
-    fused kernels the same way; fp6 e3m2 / e2m3 with M <= 16 and C % 16 == 0: the fused decode product.
-    Otherwise (larger fp6 products, fp4 rows of other lengths): the library's
+    fused kernels the same way; fp6 e3m2 / e2m3: the fused decode product for M <= 16 (C % 16 == 0) and the
+    tcgen05 GEMM above (C % 64 == 0).  Otherwise (fp6 / fp4 rows of other lengths): the library's
     dequantisation to float32 on the device, then a float32 library GEMM (the reference's own qmatmul order,
     apsi/precision.py:294-299)."""
     import torch
@@ -401,7 +401,8 @@ def _minifloat_product(x2, b, R, C, dev, out):
     fmt_id = b.kernel_format
     codes, sc = b.device_tensors(dev)
     fused = (fmt_id in (FMT_FP8_E4M3, FMT_FP8_E5M2) or (fmt_id == FMT_FP4_E2M1 and C % 128 == 0) or
-             (fmt_id in (FMT_FP6_E3M2, FMT_FP6_E2M3) and x2.shape[0] <= 16 and C % 16 == 0))
+             (fmt_id in (FMT_FP6_E3M2, FMT_FP6_E2M3) and
+              ((x2.shape[0] <= 16 and C % 16 == 0) or C % 64 == 0)))
     if fused:
         if isinstance(sc, float):
             s32 = torch.full((R,), float(np.float32(sc)), dtype=torch.float32, device=dev)

@@ -424,6 +424,9 @@ def run_ours(args, rank, world, local_rank):
     # ---- prefill GEMM, configs[2] (rank 0 reports)
     out["gemm"] = gemm_measure(torch, Kn, FMT_INT4_G128, dev, tf_peak, peak_kind)
 
+    # ---- the quantise / pack kernel (bandwidth-bound), configs[1]'s weight
+    out["quant"] = quant_measure(torch, Kn, dev, hbm_peak, peak_kind)
+
     # ---- the 70B-shaped MLP, column-sharded over all ranks (strong scaling)
     out["mlp70b"] = mlp70b_measure(torch, Kn, FMT_INT4_G128, dev, rank, world, stream, hbm_peak, tf_peak, peak_kind)
 
@@ -445,6 +448,37 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         print(json.dumps(out), flush=True)
     return 0
+
+
+def quant_measure(torch, Kn, dev, hbm_peak, peak_kind, reps=20):
+    """lb_quant_int4_g128 on configs[1]'s [11008, 4096] weight from float32 and from bfloat16, rotating over
+    weight copies larger than L2 together: algorithmic bytes (read the weight, write codes + fp16 scales) per
+    second against the HBM peak.  The float32 scales are not requested (as the layer stores fp16 scales)."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    res = {"workload": f"configs[1] weight [{N1},{K1}] -> int4-g128 codes + fp16 scales"}
+    for name, dt, esize in (("f32", torch.float32, 4), ("bf16", torch.bfloat16, 2)):
+        copies = max(2, -(-2 * L2_BYTES // (N1 * K1 * esize)))
+        ws = [(torch.randn((N1, K1), generator=gen, device=dev) * 0.02).to(dt) for _ in range(copies)]
+        outs = [Kn.quant_int4_g128(w, want_scale32=False) for w in ws]            # warm; allocates outputs
+        del outs
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(reps):
+            Kn.quant_int4_g128(ws[i % copies], want_scale32=False)
+        b.record()
+        torch.cuda.synchronize(dev)
+        s_ = a.elapsed_time(b) * 1e-3 / reps
+        nbytes = N1 * K1 * esize + weight_bytes(N1, K1)
+        gbs = nbytes / s_ / 1e9
+        res[name] = {"us_per_call": round(s_ * 1e6, 2), "GB_per_s": round(gbs, 1),
+                     "roofline": {"kernel": "quant_int4_g128_kernel", "bound": "hbm", "achieved": round(gbs, 1),
+                                  "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                                  "peak_source": f"{peak_kind} hbm_gbs",
+                                  "algorithmic_bytes_per_launch": nbytes}}
+        del ws
+    return res
 
 
 def gemm_measure(torch, Kn, fmt, dev, tf_peak, peak_kind, reps=20):

@@ -55,7 +55,8 @@ def test_bad_arguments_are_rejected_before_launch(lib):
     assert lib.lb_quant_int4_g128(fake, 7, 4, 128, fake, fake, null, null) == _lib.LB_E_ARG     # dtype
     assert lib.lb_quant_int8_rows(fake, 0, 0, 64, fake, fake, null, null) == _lib.LB_E_ARG      # N = 0
     assert lib.lb_linear(3, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_UNSUPPORTED
-    assert lib.lb_linear(7, fake, 32, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_UNSUPPORTED
+    assert lib.lb_linear(7, fake, 32, 80, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_UNSUPPORTED
+    assert lib.lb_linear(7, fake, 32, 128, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_WORKSPACE
     assert lib.lb_linear(8, fake, 1, 40, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ARG  # K % 16
     assert lib.lb_linear(2, fake, 1, 100, fake, fake, 4, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ARG
     assert lib.lb_linear(2, fake, 1, 128, fake, fake, 8, null, 0, fake, 4, null, 0, null) == _lib.LB_E_ARG  # ldy
@@ -93,7 +94,8 @@ def test_workspace_query(lib):
     assert lib.lb_linear_workspace_size(9, 16, 4, 128, ctypes.byref(n)) == 0 and n.value == 0   # fp4: decode GEMV
     assert lib.lb_linear_workspace_size(9, 17, 4, 128, ctypes.byref(n)) == 0 and n.value > 0    # fp4: GEMM
     assert lib.lb_linear_workspace_size(7, 16, 4, 128, ctypes.byref(n)) == 0 and n.value == 0   # fp6: decode
-    assert lib.lb_linear_workspace_size(8, 17, 4, 128, ctypes.byref(n)) == _lib.LB_E_UNSUPPORTED  # no fp6 GEMM
+    assert lib.lb_linear_workspace_size(8, 17, 4, 128, ctypes.byref(n)) == 0 and n.value > 0    # fp6: GEMM
+    assert lib.lb_linear_workspace_size(8, 17, 4, 80, ctypes.byref(n)) == _lib.LB_E_UNSUPPORTED   # K % 64
     assert lib.lb_linear_rms_workspace_size(2, 16, 4096, 4096, ctypes.byref(n)) == 0 and n.value == 0
     g = ctypes.c_size_t(0)
     assert lib.lb_linear_workspace_size(2, 2048, 4096, 4096, ctypes.byref(g)) == 0

@@ -150,11 +150,13 @@ def test_fp4_through_the_c_abi(cuda):
 
 @pytest.mark.parametrize("name", ["fp6_e3m2", "fp6_e2m3"])
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 300, 1040), (8, 1000, 11008), (16, 520, 2048),
-                                   (1, 77, 16), (64, 300, 512)])
+                                   (1, 77, 16), (64, 300, 512), (17, 520, 1024), (300, 1000, 4096),
+                                   (2048, 1536, 4096), (40, 260, 1040)])
 def test_fp6_fused_product_matches_oracle(cuda, name, M, N, K):
     """Per-row fp6 weights: the fused decode product for M <= 16 (four codes per three bytes, exact fp16
-    through the hardware conversion, float32 accumulation on the CUDA cores), dequantise-then-GEMM above; both
-    against the float64 product of the oracle's dequantised weights with the layer tolerance."""
+    through the hardware conversion, float32 accumulation on the CUDA cores), the tcgen05 GEMM above (codes to
+    exact fp16 in the dequantising warps; K % 64 == 0) and dequantise-then-GEMM for other K; all against the
+    float64 product of the oracle's dequantised weights with the layer tolerance."""
     import torch
     from apsi_b200 import precision as P
     rng = np.random.default_rng(M * 5 + N + K)
@@ -173,7 +175,8 @@ def test_fp6_fused_product_matches_oracle(cuda, name, M, N, K):
 @pytest.mark.parametrize("name", ["fp6_e3m2", "fp6_e2m3"])
 def test_fp6_through_the_c_abi(cuda, name):
     """lb_linear on fp6 codes straight from lb_quant_minifloat, with bias and accumulation; column shards are
-    bit-identical to the full product; repeated calls give the same bits; M > 16 is LB_E_UNSUPPORTED."""
+    bit-identical to the full product, on the decode product and on the tcgen05 GEMM; repeated calls give the same
+    bits; M > 16 with K % 64 != 0 is LB_E_UNSUPPORTED."""
     import torch
     from apsi_b200 import kernels as K
     from apsi_b200._lib import MINIFLOAT_FMT, LB_E_UNSUPPORTED, LowbitError
@@ -199,8 +202,18 @@ def test_fp6_through_the_c_abi(cuda, name):
         part = K.linear(f, x, cv[r * half:(r + 1) * half].contiguous(), s32[r * half:(r + 1) * half].contiguous(),
                         half)
         assert torch.equal(part, full[:, r * half:(r + 1) * half])
+    xg = torch.randn((300, Kd), generator=g, device=cuda).to(torch.bfloat16)    # the tcgen05 GEMM
+    yg = K.linear(f, xg, codes, s32, N)
+    refg = xg.float() @ Wd.t()
+    assert float((yg.float() - refg).abs().max()) <= 1e-2 * float(refg.abs().max())
+    for r in range(2):
+        part = K.linear(f, xg, cv[r * half:(r + 1) * half].contiguous(), s32[r * half:(r + 1) * half].contiguous(),
+                        half)
+        assert torch.equal(part, yg[:, r * half:(r + 1) * half])
+    K2 = 1040                                                                    # K % 64 != 0: no GEMM
+    c2, s2 = K.quant_minifloat(torch.randn((N, K2), generator=g, device=cuda), f, True)
     with pytest.raises(LowbitError) as e:
-        K.linear(f, torch.zeros((17, Kd), dtype=torch.bfloat16, device=cuda), codes, s32, N)
+        K.linear(f, torch.zeros((17, K2), dtype=torch.bfloat16, device=cuda), c2, s2, N)
     assert e.value.code == LB_E_UNSUPPORTED
 
 

@@ -26,8 +26,8 @@ def test_noalloc_rejects_shapes_beyond_the_scratch(lib):
     assert b"scratch" in lib.lb_last_error()
     rc = lib.lb_linear_noalloc(3, fake, 1, 128, fake, fake, 4, null, 0, fake, 4, null)    # g32: no product
     assert rc == _lib.LB_E_UNSUPPORTED
-    rc = lib.lb_linear_noalloc(7, fake, 17, 128, fake, fake, 4, null, 0, fake, 4, null)   # fp6: decode only
-    assert rc == _lib.LB_E_UNSUPPORTED
+    rc = lib.lb_linear_noalloc(7, fake, 17, 80, fake, fake, 4, null, 0, fake, 4, null)    # fp6 above M = 16:
+    assert rc == _lib.LB_E_UNSUPPORTED                                                    # K % 64 == 0 only
 
 
 def _ptr(t):
