@@ -307,11 +307,11 @@ except AttributeError:                                 # pragma: no cover
     _cur_dev = None
 
 
-def linear_spec(spec, x, out=None):
+def linear_spec(spec, x, out=None, static_weights=False):
     """``linear`` for a weight described by ``spec`` = (fmt, codes pointer, scales pointer, N, K, device index)
     and a contiguous bfloat16 CUDA x [M, K] on the current device, in the fewest host operations: the per-call
-    path of ``precision.qmatmul``.  Returns None (the caller takes the general path) when x, out or the device
-    do not fit it."""
+    path of ``precision.qmatmul``.  ``static_weights`` as in ``linear``.  Returns None (the caller takes the
+    general path) when x, out or the device do not fit it."""
     fmt, cptr, sptr, N, K, dev = spec
     if _raw_stream is None or x.shape[1] != K or not x.is_contiguous() or x.get_device() != dev or _cur_dev() != dev:
         return None
@@ -323,7 +323,7 @@ def linear_spec(spec, x, out=None):
     elif out.dim() != 2 or out.shape[0] != M or out.shape[1] != N or out.stride(1) != 1 or out.dtype != x.dtype:
         return None
     rc = _fn("lb_linear_ex")(fmt, x.data_ptr(), M, K, cptr, sptr, N, None, 0, out.data_ptr(), out.stride(0), None,
-                             0, 0, _raw_stream(dev))
+                             0, _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0, _raw_stream(dev))
     if rc:
         _lib.check(rc)
     return out

@@ -81,7 +81,7 @@ class QTensor:
     scales the kernels read), ``group`` (128 for int4 groups, None for one scale per row), ``kn`` (True when
     the logical array is ``[in, out]`` and the rows stored are its transpose, see ``quantize_linear``)."""
     __slots__ = ("codes", "scale", "fmt", "shape", "axis", "dim", "packed", "scale16", "group", "kn", "_dev",
-                 "_fast")
+                 "_fast", "_settled")
     # NumPy defers ``x @ q`` (and every other binary operator) to this class, so a model written with plain
     # ``x @ p.W`` -- the reference's Linear.apply (apsi/layers.py:251-253), its attention and SwiGLU blocks --
     # multiplies a QTensor weight through __rmatmul__ and the fused kernels, unchanged
@@ -93,6 +93,12 @@ class QTensor:
         self.scale16, self.group, self.kn = scale16, group, kn
         self._dev = None
         self._fast = None
+        self._settled = False
+
+    def touch(self):
+        """Call after writing into ``codes`` / ``scale16`` in place: the next product waits for every earlier
+        kernel before it reads the weights (see ``qmatmul``)."""
+        self._settled = False
 
     def fast_spec(self):
         """(fmt, codes pointer, scales pointer, N, K, device index) for the per-call fast path of ``qmatmul``, or
@@ -102,6 +108,7 @@ class QTensor:
         f = self._fast
         if f is not None and f[0] is c and f[1] is s16:
             return f[2]
+        self._settled = False                  # new weight tensors: their writer may still be running
         spec = None
         if self.fmt.kind == "int" and _is_torch(c) and c.is_cuda and s16 is not None and s16.is_cuda:
             R, C = self.rows
@@ -335,6 +342,12 @@ def dequantize(q):
 def qmatmul(a, b, out=None):
     """``a @ b`` with a quantised right operand on the fused kernels (apsi/precision.py:294-299).
 
+    The weights of a device QTensor are treated as static from its second decode product on: that launch
+    streams them before the previous kernel on the stream has finished (programmatic dependent launch; the
+    activations and the output still wait for it).  The first product after the QTensor's weight tensors were
+    set runs without it, so the kernel that wrote them has completed.  After writing into ``codes`` or
+    ``scale16`` in place, call ``b.touch()``.
+
     ``b`` must be a QTensor in the kernel layout (``quantize_linear``, or ``quantize(W, ..., axis=0)`` of a
     ``[N, K]`` weight, which multiplies as ``a @ W.T`` -- the hub / HF orientation).  ``a`` is ``[..., K]``:
     a CUDA tensor stays on the device (bfloat16 out); NumPy / CPU inputs are copied in and the result copied
@@ -344,8 +357,9 @@ def qmatmul(a, b, out=None):
     if type(b) is QTensor and type(a) is _TORCH_TENSOR[0]:
         spec = b.fast_spec()
         if spec is not None and a.dtype is _TORCH_TENSOR[1] and a.dim() == 2 and a.is_cuda:
-            y = _k.linear_spec(spec, a, out)
+            y = _k.linear_spec(spec, a, out, b._settled)
             if y is not None:
+                b._settled = True
                 return y
     import torch
     if isinstance(a, QTensor):

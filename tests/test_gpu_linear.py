@@ -208,3 +208,27 @@ def test_qmatmul_fast_path_matches_general_path(cuda):
     q2 = P.quantize(W * 2, "int4", axis=0, group=128)
     q.codes, q.scale16 = q2.codes, q2.scale16                # replaced tensors: the cached spec is rebuilt
     assert torch.equal(P.qmatmul(x, q), P.qmatmul(x.unsqueeze(0), q2)[0])
+
+
+def test_qmatmul_streams_settled_weights_early(cuda):
+    """From a QTensor's second decode product on, precision.qmatmul launches with static weights (the weight
+    stream starts before the previous kernel ends): same bits as the first, plain launch; after an in-place
+    rewrite of the weights, touch() makes the next product wait for the writer again."""
+    import torch
+    from apsi_b200 import precision as P
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    W1 = torch.randn((3000, 4096), generator=g, device=cuda) * 0.02
+    W2 = torch.randn((3000, 4096), generator=g, device=cuda) * 0.02
+    x = torch.randn((2, 4096), generator=g, device=cuda).to(torch.bfloat16)
+    q = P.quantize(W1, "int4", axis=0, group=128)
+    assert not q._settled
+    y1 = P.qmatmul(x, q)
+    assert q._settled
+    assert torch.equal(P.qmatmul(x, q), y1)
+    q2 = P.quantize(W2, "int4", axis=0, group=128)
+    q.codes.copy_(q2.codes)
+    q.scale16.copy_(q2.scale16)
+    q.touch()
+    y2 = P.qmatmul(x, q)
+    assert torch.equal(y2, P.qmatmul(x, q2))

@@ -61,7 +61,7 @@ def _worker(rank, world, port, M, N, K, out_dir, mode="nccl"):
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("M,N,K", [(1, 11008, 4096), (4, 4096, 11008), (64, 2048, 4096), (1, 8192, 28672),
-                                   (64, 28672, 8192)])
+                                   (64, 28672, 8192), (64, 8192, 28672)])
 def test_column_shards_match_unsharded_bits(tmp_path, M, N, K, mode, world):
     """Every rank's assembled [M, N] output equals the unsharded product bit for bit, at 2, 4 and 8 ranks (as
     many as the machine has GPUs), over three calls (both p2p output buffers)."""
