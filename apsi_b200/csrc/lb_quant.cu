@@ -67,36 +67,50 @@ __device__ __forceinline__ float absmax_scale(float m, float qmax) {
 }
 
 // ------------------------------------------------------------------------------------------- int4, g128
-// 16 threads per group of 128 values (8 each), so a warp quantises two groups per step.
+// 16 threads per group of 128 values (8 each), so a warp quantises two groups per step; each half-warp loads
+// two groups before it quantises either, so twice the bytes are in flight per thread (the kernel is bound by
+// loads in flight, not arithmetic).  Shuffles name only the half-warp's own lanes: the two halves of a warp may
+// leave the loop at different steps.
+template <int DT>
+__device__ __forceinline__ void quant_group_g128(const float (&v)[8], int64_t g, int sub, unsigned half_mask,
+                                                 uint32_t* __restrict__ packed, __half* __restrict__ scale16,
+                                                 float* __restrict__ scale32) {
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(half_mask, m, o, 16));
+  const float s = absmax_scale(m, 7.0f);
+  const float inv = 1.0f / s;
+  uint32_t word = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float q = fminf(fmaxf(round_quot(v[j], s, inv), -7.f), 7.f);
+    word |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xFu) << (4 * j);
+  }
+  packed[g * 16 + sub] = word;
+  if (sub == 0) {
+    scale16[g] = __float2half_rn(s);
+    if (scale32) scale32[g] = s;
+  }
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) quant_int4_g128_kernel(const void* __restrict__ w, int64_t ngroups,
                                                               uint32_t* __restrict__ packed,
                                                               __half* __restrict__ scale16,
                                                               float* __restrict__ scale32) {
   const int sub = threadIdx.x & 15;
+  const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
   int64_t g = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
   const int64_t gstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
-  for (; g < ngroups; g += gstride) {  // uniform per 16-lane half-warp
-    float v[8];
+  for (; g < ngroups; g += 2 * gstride) {  // uniform per 16-lane half-warp
+    const int64_t g2 = g + gstride;
+    float v[8], v2[8];
     load_w8<DT>(w, g * 128 + sub * 8, v);
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
-#pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 16));
-    const float s = absmax_scale(m, 7.0f);
-    const float inv = 1.0f / s;
-    uint32_t word = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float q = fminf(fmaxf(round_quot(v[j], s, inv), -7.f), 7.f);
-      word |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xFu) << (4 * j);
-    }
-    packed[g * 16 + sub] = word;
-    if (sub == 0) {
-      scale16[g] = __float2half_rn(s);
-      if (scale32) scale32[g] = s;
-    }
+    if (g2 < ngroups) load_w8<DT>(w, g2 * 128 + sub * 8, v2);
+    quant_group_g128<DT>(v, g, sub, half_mask, packed, scale16, scale32);
+    if (g2 < ngroups) quant_group_g128<DT>(v2, g2, sub, half_mask, packed, scale16, scale32);
   }
 }
 
@@ -152,14 +166,15 @@ __global__ void __launch_bounds__(256) quant_int8_rows_kernel(const void* __rest
 // scale = (first value of largest magnitude)/-8, codes stored as q + 8.  float32 arithmetic as qnumpy.
 // Scale of one block of 32 values held 8 per thread by 4 consecutive lanes (sub = lane % 4), float32 as
 // hub_gpu.qnumpy: int8 max|v| / 127; int4 the signed value of the first largest magnitude / -8.
+// `quad` names the four lanes of the block (the quads of a warp may leave their loop at different steps).
 template <int KIND>
-__device__ __forceinline__ float g32_scale(const float (&v)[8], int sub) {
+__device__ __forceinline__ float g32_scale(const float (&v)[8], int sub, unsigned quad) {
   if (KIND == 8) {
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
 #pragma unroll
-    for (int o = 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 4));
+    for (int o = 2; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(quad, m, o, 4));
     return __fdiv_rn(m, 127.0f);
   }
   // first index of the largest magnitude (numpy argmax), then its signed value
@@ -172,9 +187,9 @@ __device__ __forceinline__ float g32_scale(const float (&v)[8], int sub) {
   }
 #pragma unroll
   for (int o = 2; o >= 1; o >>= 1) {
-    float oam = __shfl_xor_sync(0xffffffffu, am, o, 4);
-    float omv = __shfl_xor_sync(0xffffffffu, mv, o, 4);
-    int oidx = __shfl_xor_sync(0xffffffffu, idx, o, 4);
+    float oam = __shfl_xor_sync(quad, am, o, 4);
+    float omv = __shfl_xor_sync(quad, mv, o, 4);
+    int oidx = __shfl_xor_sync(quad, idx, o, 4);
     if (oam > am || (oam == am && oidx < idx)) { am = oam; mv = omv; idx = oidx; }
   }
   return __fdiv_rn(mv, -8.0f);
@@ -185,12 +200,13 @@ __global__ void __launch_bounds__(256) quant_g32_kernel(const void* __restrict__
                                                         uint32_t* __restrict__ words,
                                                         float* __restrict__ scale32) {
   const int sub = threadIdx.x & 3;
+  const unsigned quad = 0xFu << (threadIdx.x & 28);
   int64_t b = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 2;
   const int64_t bstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 2;
   for (; b < nblocks; b += bstride) {
     float v[8];
     load_w8<DT>(w, b * 32 + sub * 8, v);
-    const float sc = g32_scale<KIND>(v, sub);
+    const float sc = g32_scale<KIND>(v, sub, quad);
     const float inv = (sc != 0.f) ? __fdiv_rn(1.0f, sc) : 0.f;
     uint32_t out0 = 0, out1 = 0;
 #pragma unroll
@@ -222,12 +238,13 @@ template <int DT, int KIND>
 __global__ void __launch_bounds__(256) round_g32_kernel(const void* __restrict__ w, int64_t nblocks,
                                                         float* __restrict__ out) {
   const int sub = threadIdx.x & 3;
+  const unsigned quad = 0xFu << (threadIdx.x & 28);
   int64_t b = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 2;
   const int64_t bstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 2;
   for (; b < nblocks; b += bstride) {
     float v[8];
     load_w8<DT>(w, b * 32 + sub * 8, v);
-    const float sc = g32_scale<KIND>(v, sub);
+    const float sc = g32_scale<KIND>(v, sub, quad);
     const float inv = (sc != 0.f) ? __fdiv_rn(1.0f, sc) : 0.f;
     const float lo = KIND == 8 ? -127.f : -8.f, hi = KIND == 8 ? 127.f : 7.f;
     float d[8];
