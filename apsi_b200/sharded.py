@@ -113,7 +113,10 @@ class PeerOutputs:
 
     def finish(self):
         """Barrier: every rank's stores of this call are visible on every rank (on the current stream).  The
-        barrier's epoch comes from the device-side counter, so the call may be captured in a CUDA graph."""
+        barrier's epoch comes from the device-side counter, so its flags stay in step when a CUDA graph replays
+        it.  The choice between the two output buffers is made on the host (``out``), so a captured graph
+        replays into the buffers it was captured with: capture two consecutive calls (one per buffer) in one
+        graph, or a faster rank's next replay may overwrite columns a slower rank is still reading."""
         self.epoch += 1
         kernels.rank_barrier(self.ptrs[2], self.rank, 0, self.device, self.timeout_ms)
 
