@@ -188,6 +188,93 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const uint16_t* __restrict_
   }
 }
 
+// The same conversion with one 256-thread block per row and the row held in registers (CH 16-byte chunks per
+// thread, rows of up to CH * 2048 values): x is read from HBM once, not twice, and a row's loads are all in
+// flight together.  The factor and every converted value are those of prep_x_kernel (the maximum does not
+// depend on the order it is taken in).
+template <int PERM>
+__device__ __forceinline__ uint4 prep_chunk(uint4 v, float down) {
+  const uint32_t r[4] = {v.x, v.y, v.z, v.w};
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = __uint_as_float(r[j] << 16) * down;
+    f[2 * j + 1] = __uint_as_float(r[j] & 0xFFFF0000u) * down;
+  }
+  float g[8];
+  if (PERM == 0) {
+    g[0] = f[0]; g[1] = f[4]; g[2] = f[1]; g[3] = f[5]; g[4] = f[2]; g[5] = f[6]; g[6] = f[3]; g[7] = f[7];
+  } else if (PERM == 2) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = f[j];
+  } else {
+    g[0] = f[0]; g[1] = f[2]; g[2] = f[1]; g[3] = f[3]; g[4] = f[4]; g[5] = f[6]; g[6] = f[5]; g[7] = f[7];
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 h = __floats2half2_rn(g[2 * j], g[2 * j + 1]);
+    o[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int PERM, int CH>
+__global__ void __launch_bounds__(256) prep_x_rows_kernel(const uint16_t* __restrict__ x, int64_t K,
+                                                          uint16_t* __restrict__ x16, float* __restrict__ tokscale) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const int nch = static_cast<int>(K / 8);
+  const uint16_t* xr = x + row * K;
+  uint4 v[CH];
+  float m = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int ch = threadIdx.x + c * 256;
+    v[c] = ch < nch ? ldg_nc_v4(xr + ch * 8) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const uint32_t r[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m = fmaxf(m, fabsf(__uint_as_float(r[j] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(r[j] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+  int e = 0;
+  if (m > 0.f) {
+    int ex;
+    frexpf(m, &ex);
+    e = ex - 15;
+    e = e < -110 ? -110 : (e > 110 ? 110 : e);
+  }
+  const float down = ldexpf(1.0f, -e);
+  if (threadIdx.x == 0) tokscale[row] = ldexpf(1.0f, e);
+  uint16_t* out = x16 + row * K;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int ch = threadIdx.x + c * 256;
+    if (ch < nch) *reinterpret_cast<uint4*>(out + ch * 8) = prep_chunk<PERM>(v[c], down);
+  }
+}
+
+template <int PERM>
+static void launch_prep_x(const uint16_t* x, int64_t M, int64_t K, uint16_t* x16, float* tokscale, cudaStream_t st) {
+  const int64_t chunks = (K / 8 + 255) / 256;                 // 16-byte chunks per thread
+  if (chunks <= 1) prep_x_rows_kernel<PERM, 1><<<static_cast<unsigned>(M), 256, 0, st>>>(x, K, x16, tokscale);
+  else if (chunks <= 2) prep_x_rows_kernel<PERM, 2><<<static_cast<unsigned>(M), 256, 0, st>>>(x, K, x16, tokscale);
+  else if (chunks <= 4) prep_x_rows_kernel<PERM, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, K, x16, tokscale);
+  else prep_x_kernel<PERM><<<static_cast<unsigned>((M + 7) / 8), 256, 0, st>>>(x, M, K, x16, tokscale);
+}
+
 // ------------------------------------------------------------------------------------------- dequantisers
 // int4: 16 bytes = 32 codes of one row (k = 8i + j for word i, nibble j) -> 16 fp16 pairs in logical K order
 // (pair 4i + p holds physical nibbles (p, p + 4) of word i), each fp16(q * s).
@@ -646,13 +733,10 @@ cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void
   float* tokscale = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + x16b);
   float* part = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ws_front_bytes(M, K));
   {
-    const unsigned blocks = static_cast<unsigned>((M + 7) / 8);
-    if (fmt == 2)
-      prep_x_kernel<0><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
-    else if (fmt == 9 || fmt == 7 || fmt == 8)     // codes in natural K order
-      prep_x_kernel<2><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
-    else
-      prep_x_kernel<1><<<blocks, 256, 0, st>>>(reinterpret_cast<const uint16_t*>(x), M, K, x16, tokscale);
+    const uint16_t* xb = reinterpret_cast<const uint16_t*>(x);
+    if (fmt == 2) launch_prep_x<0>(xb, M, K, x16, tokscale, st);
+    else if (fmt == 9 || fmt == 7 || fmt == 8) launch_prep_x<2>(xb, M, K, x16, tokscale, st);   // natural K order
+    else launch_prep_x<1>(xb, M, K, x16, tokscale, st);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

@@ -67,50 +67,43 @@ __device__ __forceinline__ float absmax_scale(float m, float qmax) {
 }
 
 // ------------------------------------------------------------------------------------------- int4, g128
-// 16 threads per group of 128 values (8 each), so a warp quantises two groups per step; each half-warp loads
-// two groups before it quantises either, so twice the bytes are in flight per thread (the kernel is bound by
-// loads in flight, not arithmetic).  Shuffles name only the half-warp's own lanes: the two halves of a warp may
-// leave the loop at different steps.
-template <int DT>
-__device__ __forceinline__ void quant_group_g128(const float (&v)[8], int64_t g, int sub, unsigned half_mask,
-                                                 uint32_t* __restrict__ packed, __half* __restrict__ scale16,
-                                                 float* __restrict__ scale32) {
-  float m = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
-#pragma unroll
-  for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(half_mask, m, o, 16));
-  const float s = absmax_scale(m, 7.0f);
-  const float inv = 1.0f / s;
-  uint32_t word = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float q = fminf(fmaxf(round_quot(v[j], s, inv), -7.f), 7.f);
-    word |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xFu) << (4 * j);
-  }
-  packed[g * 16 + sub] = word;
-  if (sub == 0) {
-    scale16[g] = __float2half_rn(s);
-    if (scale32) scale32[g] = s;
-  }
-}
-
+// 8 threads per group of 128 values (16 each: two 8-value loads), so a warp quantises four groups per step and
+// the per-group work (absmax tree, scale division, reciprocal) is shared by 16 values per thread.  The kernel is
+// bound by its instruction stream, not by HBM, at 8 values per thread.  The reciprocal only feeds round_quot's
+// estimate, which is checked against a margin (2^-10) far wider than the estimate's error and decided exactly
+// otherwise, so the fast approximate division gives the same codes.  Shuffles name only the lanes of their own
+// group: the groups of a warp may leave the loop at different steps.
 template <int DT>
 __global__ void __launch_bounds__(256) quant_int4_g128_kernel(const void* __restrict__ w, int64_t ngroups,
                                                               uint32_t* __restrict__ packed,
                                                               __half* __restrict__ scale16,
                                                               float* __restrict__ scale32) {
-  const int sub = threadIdx.x & 15;
-  const unsigned half_mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
-  int64_t g = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
-  const int64_t gstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 4;
-  for (; g < ngroups; g += 2 * gstride) {  // uniform per 16-lane half-warp
-    const int64_t g2 = g + gstride;
-    float v[8], v2[8];
-    load_w8<DT>(w, g * 128 + sub * 8, v);
-    if (g2 < ngroups) load_w8<DT>(w, g2 * 128 + sub * 8, v2);
-    quant_group_g128<DT>(v, g, sub, half_mask, packed, scale16, scale32);
-    if (g2 < ngroups) quant_group_g128<DT>(v2, g2, sub, half_mask, packed, scale16, scale32);
+  const int sub = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  int64_t g = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+  const int64_t gstride = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 3;
+  for (; g < ngroups; g += gstride) {  // uniform per 8-lane group
+    float v[2][8];
+    load_w8<DT>(w, g * 128 + sub * 16, v[0]);
+    load_w8<DT>(w, g * 128 + sub * 16 + 8, v[1]);
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(v[j >> 3][j & 7]));
+#pragma unroll
+    for (int o = 4; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(gmask, m, o, 8));
+    const float s = absmax_scale(m, 7.0f);
+    const float inv = __fdividef(1.0f, s);
+    uint32_t word[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float q = fminf(fmaxf(round_quot(v[j >> 3][j & 7], s, inv), -7.f), 7.f);
+      word[j >> 3] |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xFu) << (4 * (j & 7));
+    }
+    *reinterpret_cast<uint2*>(packed + g * 16 + sub * 2) = make_uint2(word[0], word[1]);
+    if (sub == 0) {
+      scale16[g] = __float2half_rn(s);
+      if (scale32) scale32[g] = s;
+    }
   }
 }
 
@@ -329,7 +322,7 @@ static int grid_for(int64_t work_threads, int sms) {
 cudaError_t launch_quant_int4_g128(const void* w, int dt, int64_t N, int64_t K, uint8_t* packed, uint16_t* s16,
                                    float* s32, int sms, cudaStream_t st) {
   const int64_t ng = N * (K / 128);
-  const int grid = grid_for(ng * 16, sms);
+  const int grid = grid_for(ng * 8, sms);
   if (dt == 0)
     quant_int4_g128_kernel<0><<<grid, 256, 0, st>>>(w, ng, reinterpret_cast<uint32_t*>(packed),
                                                     reinterpret_cast<__half*>(s16), s32);
