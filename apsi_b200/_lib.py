@@ -47,6 +47,9 @@ SIGNATURES = [
     ("lb_linear_workspace_size", _I, [_I, _I64, _I64, _I64, ctypes.POINTER(_SZ)]),
     ("lb_linear", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, _P]),
     ("lb_linear_ex", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P, _SZ, ctypes.c_uint, _P]),
+    ("lb_weight_create", _I, [_I, _P, _P, _I64, _I64, ctypes.POINTER(_P)]),
+    ("lb_weight_linear", _I, [_P, _P, _I64, _P, _I64, ctypes.c_uint, _P]),
+    ("lb_weight_destroy", _I, [_P]),
     ("lb_interleave_cols", _I, [_P, _I, _I64, _I64, _P, _P]),
     ("lb_linear_noalloc", _I, [_I, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I64, _P]),
     ("lb_peer_alloc", _I, [_SZ, ctypes.POINTER(_P), _P]),

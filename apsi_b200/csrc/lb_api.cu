@@ -5,6 +5,7 @@
 #include <string.h>
 #include <atomic>
 #include <mutex>
+#include <new>
 
 #include "../../include/apsi_lowbit.h"
 #include "lb_common.cuh"
@@ -358,6 +359,76 @@ int lb_linear(int fmt, const void* x, int64_t M, int64_t K, const void* codes, c
               const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
               void* stream) {
   return lb_linear_ex(fmt, x, M, K, codes, scales, N, bias, accumulate, y, ldy, workspace, ws_bytes, 0u, stream);
+}
+
+// A weight prepared for repeated decode products: everything lb_linear_ex checks about the weight is checked
+// once, and the tensor maps of its stream are encoded once; a call then checks x, y and the device and launches.
+struct lb_weight {
+  int fmt;
+  const void* codes;
+  const void* scales;
+  int64_t N, K;
+  int dev, sms;
+  GemvMaps maps;
+};
+
+int lb_weight_create(int fmt, const void* codes, const void* scales, int64_t N, int64_t K, lb_weight** out) {
+  if (!out) return fail(LB_E_ARG, "lb_weight_create: out is NULL");
+  *out = nullptr;
+  if (!has_product(fmt))
+    return fail(LB_E_UNSUPPORTED, "lb_weight_create: format %d has no product kernel in this build", fmt);
+  if (!codes || !scales) return fail(LB_E_ARG, "lb_weight_create: codes and scales are required");
+  if (N <= 0 || K <= 0) return fail(LB_E_ARG, "lb_weight_create: N and K must be positive");
+  if (N > (1LL << 31)) return fail(LB_E_ARG, "lb_weight_create: N must be below 2^31");
+  const int64_t kmult = (fmt == LB_FMT_INT4_G128 || fmt == LB_FMT_FP4_E2M1) ? 128 : (is_fp6(fmt) ? 16 : 64);
+  if (K % kmult) return fail(LB_E_ARG, "lb_weight_create: K (%lld) must be a multiple of %lld", (long long)K, (long long)kmult);
+  if (K > gemv_max_k(fmt))
+    return fail(LB_E_UNSUPPORTED, "lb_weight_create: K (%lld) above %d is not supported for M <= 16", (long long)K,
+                gemv_max_k(fmt));
+  if (!aligned(codes, 16) || !aligned(scales, 16))
+    return fail(LB_E_ALIGN, "lb_weight_create: codes and scales must be 16-byte aligned");
+  DevInfo* d;
+  int r = current(&d);
+  if (r) return r;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  lb_weight* w = new (std::nothrow) lb_weight;
+  if (!w) return fail(LB_E_ARG, "lb_weight_create: out of host memory");
+  w->fmt = fmt;
+  w->codes = codes;
+  w->scales = scales;
+  w->N = N;
+  w->K = K;
+  w->dev = dev;
+  w->sms = d->sms;
+  prepare_gemv_maps(fmt, codes, scales, N, K, &w->maps);
+  *out = w;
+  return LB_OK;
+}
+
+int lb_weight_linear(const lb_weight* w, const void* x, int64_t M, void* y, int64_t ldy, unsigned flags,
+                     void* stream) {
+  if (!w) return fail(LB_E_ARG, "lb_weight_linear: the weight is NULL");
+  if (M <= 0) return fail(LB_E_ARG, "lb_weight_linear: M must be positive");
+  if (!use_gemv(M))
+    return fail(LB_E_UNSUPPORTED, "lb_weight_linear: M (%lld) above 16 needs lb_linear with a workspace", (long long)M);
+  if (flags & ~static_cast<unsigned>(LB_LINEAR_STATIC_WEIGHTS)) return fail(LB_E_ARG, "lb_weight_linear: unknown flags");
+  if (!x || !y) return fail(LB_E_ARG, "lb_weight_linear: x and y are required");
+  if (ldy < w->N) return fail(LB_E_ARG, "lb_weight_linear: ldy (%lld) < N (%lld)", (long long)ldy, (long long)w->N);
+  if (!aligned(x, 16) || !aligned(y, 2)) return fail(LB_E_ALIGN, "lb_weight_linear: x must be 16-byte and y 2-byte aligned");
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != w->dev)
+    return fail(LB_E_DEVICE, "lb_weight_linear: the weight was prepared on device %d, the current device is %d", w->dev,
+                dev);
+  return launched(launch_gemv(w->fmt, x, M, w->K, w->codes, w->scales, w->N, nullptr, 0, y, ldy, w->sms,
+                              (flags & LB_LINEAR_STATIC_WEIGHTS) != 0, static_cast<cudaStream_t>(stream), nullptr,
+                              nullptr, &w->maps),
+                  "gemv");
+}
+
+int lb_weight_destroy(lb_weight* w) {
+  delete w;
+  return LB_OK;
 }
 
 static size_t rms_rows_bytes(int64_t M, int64_t K) { return (static_cast<size_t>(M) * K * 2 + 255) & ~static_cast<size_t>(255); }

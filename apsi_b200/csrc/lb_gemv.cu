@@ -1163,9 +1163,19 @@ static bool encode_gemv_boxes(const void* codes, const void* scales, int64_t N, 
   return true;
 }
 
+void prepare_gemv_maps(int fmt, const void* codes, const void* scales, int64_t N, int64_t K, GemvMaps* m) {
+  m->ok = 0;
+  m->stma = 0;
+  bool stma = false;
+  if (fmt == 2 && encode_gemv_boxes(codes, scales, N, K, true, &m->tw, &m->ts, &stma)) {
+    m->ok = 1;
+    m->stma = stma ? 1 : 0;
+  }
+}
+
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st, const OutRanks* dst, const RmsPrologue* ln) {
+                        cudaStream_t st, const OutRanks* dst, const RmsPrologue* ln, const GemvMaps* maps) {
   GemvParams p;
   p.x = reinterpret_cast<const uint16_t*>(x);
   p.w = reinterpret_cast<const uint8_t*>(codes);
@@ -1212,10 +1222,16 @@ cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void
     if (M <= 2) {
       // box mode: one tensor copy per item (codes, and scales when their rows allow it); three groups, one slot
       // each ([28672, 8192]: 31.7 -> 29.2 us, [8192, 28672]: 40.3 -> 36.7 us against one copy per row)
-      CUtensorMap tw, ts;
-      bool stma = false;
-      if (encode_gemv_boxes(codes, scales, N, K, true, &tw, &ts, &stma)) {
-        p.scale_tma = stma ? 1 : 0;
+      // a prepared weight brings its maps (encoded once); otherwise they are encoded for this launch
+      GemvMaps local;
+      if (!maps) {
+        prepare_gemv_maps(fmt, codes, scales, N, K, &local);
+        maps = &local;
+      }
+      const CUtensorMap& tw = maps->tw;
+      const CUtensorMap& ts = maps->ts;
+      if (maps->ok) {
+        p.scale_tma = maps->stma;
         // one or two K ranges per row and a row block for every SM: six slots, so a CTA requests (almost) its
         // whole share of the weights at once, with the codes read from the slot unit by unit
         // ([11008, 4096]: 7.15 -> 6.68 us, [28672, 8192]: 25.1 -> 23.4 us); otherwise three slots

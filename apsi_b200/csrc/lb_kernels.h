@@ -1,5 +1,6 @@
 // Internal launchers (host side) shared between the kernel files and the C ABI in lb_api.cu.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -35,9 +36,19 @@ struct RmsPrologue {
   float eps, off;
 };
 
+// The tensor maps of an int4 weight's stream (box mode of the decode GEMV), encoded once for a prepared weight.
+// ok == 0: no maps (the launch takes the row-copy path, as when encoding fails).
+struct GemvMaps {
+  int ok;
+  int stma;                  // the scales have a tensor map too
+  CUtensorMap tw, ts;
+};
+void prepare_gemv_maps(int fmt, const void* codes, const void* scales, int64_t N, int64_t K, GemvMaps* m);
+
 cudaError_t launch_gemv(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,
                         int64_t N, const void* bias, int acc, void* y, int64_t ldy, int sms, bool pdl,
-                        cudaStream_t st, const OutRanks* dst = nullptr, const RmsPrologue* ln = nullptr);
+                        cudaStream_t st, const OutRanks* dst = nullptr, const RmsPrologue* ln = nullptr,
+                        const GemvMaps* maps = nullptr);
 
 size_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 cudaError_t launch_gemm(int fmt, const void* x, int64_t M, int64_t K, const void* codes, const void* scales,

@@ -14,7 +14,8 @@ from ._lib import FMT_INT8_ROW, FMT_INT4_G128, FMT_Q8_0_G32, FMT_Q4_0_G32, DT_F3
 __all__ = ["quant_int8_rows", "quant_int4_g128", "quant_q8_0_g32", "quant_q4_0_g32", "round_g32", "dequant", "linear",
            "linear_workspace_bytes", "interleave_cols", "device_errors", "FMT_INT8_ROW", "FMT_INT4_G128",
            "FMT_Q8_0_G32", "FMT_Q4_0_G32", "LowbitError", "minifloat_bytes", "quant_minifloat", "dequant_minifloat",
-           "gguf_encode", "gguf_decode", "linear_spec"]
+           "gguf_encode", "gguf_decode", "linear_spec",
+           "prepare_weight", "PreparedWeight"]
 
 
 def _ptr(t):
@@ -307,12 +308,40 @@ except AttributeError:                                 # pragma: no cover
     _cur_dev = None
 
 
+class PreparedWeight:
+    """An ``lb_weight`` handle: a weight checked once, with the tensor maps of its stream encoded once, for the
+    per-call decode product (``lb_weight_linear``).  It holds the pointers of the codes and scales, not the
+    tensors: the owner keeps them alive (a QTensor holds both).  Destroyed with the object."""
+    __slots__ = ("ptr", "_destroy")
+
+    def __init__(self, fmt, cptr, sptr, N, K, dev):
+        self.ptr = None
+        self._destroy = _fn("lb_weight_destroy")
+        h = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            _lib.call("lb_weight_create", fmt, cptr, sptr, N, K, ctypes.byref(h))
+        self.ptr = h.value
+
+    def __del__(self):
+        p, self.ptr = self.ptr, None
+        if p:
+            self._destroy(p)
+
+
+def prepare_weight(fmt, cptr, sptr, N, K, dev):
+    """A ``PreparedWeight``, or None when the weight has no decode product (the caller uses ``lb_linear_ex``)."""
+    try:
+        return PreparedWeight(fmt, cptr, sptr, N, K, dev)
+    except _lib.LowbitError:
+        return None
+
+
 def linear_spec(spec, x, out=None, static_weights=False):
-    """``linear`` for a weight described by ``spec`` = (fmt, codes pointer, scales pointer, N, K, device index)
-    and a contiguous bfloat16 CUDA x [M, K] on the current device, in the fewest host operations: the per-call
-    path of ``precision.qmatmul``.  ``static_weights`` as in ``linear``.  Returns None (the caller takes the
-    general path) when x, out or the device do not fit it."""
-    fmt, cptr, sptr, N, K, dev = spec
+    """``linear`` for a weight described by ``spec`` = (fmt, codes pointer, scales pointer, N, K, device index,
+    PreparedWeight or None) and a contiguous bfloat16 CUDA x [M, K] on the current device, in the fewest host
+    operations: the per-call path of ``precision.qmatmul``.  ``static_weights`` as in ``linear``.  Returns None
+    (the caller takes the general path) when x, out or the device do not fit it."""
+    fmt, cptr, sptr, N, K, dev, pw = spec
     if _raw_stream is None or x.shape[1] != K or not x.is_contiguous() or x.get_device() != dev or _cur_dev() != dev:
         return None
     M = x.shape[0]
@@ -322,8 +351,12 @@ def linear_spec(spec, x, out=None, static_weights=False):
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     elif out.dim() != 2 or out.shape[0] != M or out.shape[1] != N or out.stride(1) != 1 or out.dtype != x.dtype:
         return None
-    rc = _fn("lb_linear_ex")(fmt, x.data_ptr(), M, K, cptr, sptr, N, None, 0, out.data_ptr(), out.stride(0), None,
-                             0, _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0, _raw_stream(dev))
+    flags = _lib.LINEAR_STATIC_WEIGHTS if static_weights else 0
+    if pw is not None:
+        rc = _fn("lb_weight_linear")(pw.ptr, x.data_ptr(), M, out.data_ptr(), out.stride(0), flags, _raw_stream(dev))
+    else:
+        rc = _fn("lb_linear_ex")(fmt, x.data_ptr(), M, K, cptr, sptr, N, None, 0, out.data_ptr(), out.stride(0),
+                                 None, 0, flags, _raw_stream(dev))
     if rc:
         _lib.check(rc)
     return out

@@ -112,7 +112,8 @@ class QTensor:
         spec = None
         if self.fmt.kind == "int" and _is_torch(c) and c.is_cuda and s16 is not None and s16.is_cuda:
             R, C = self.rows
-            spec = (self.kernel_format, c.data_ptr(), s16.data_ptr(), R, C, c.get_device())
+            fmt, cp, sp, dev = self.kernel_format, c.data_ptr(), s16.data_ptr(), c.get_device()
+            spec = (fmt, cp, sp, R, C, dev, _k.prepare_weight(fmt, cp, sp, R, C, dev))
         self._fast = (c, s16, spec)
         return spec
 

@@ -230,6 +230,21 @@ int lb_linear_ex(int fmt, const void* x, int64_t M, int64_t K, const void* codes
                  const void* bias, int accumulate, void* y, int64_t ldy, void* workspace, size_t ws_bytes,
                  unsigned flags, void* stream);
 
+/* A weight prepared for repeated decode products (M <= 16).  lb_weight_create checks the format, codes, scales
+ * and shape once, as lb_linear_ex would, on the current device, and encodes the tensor maps of the weight
+ * stream once.  lb_weight_linear(w, x, M, y, ldy, flags, stream) then gives the bits of
+ * lb_linear_ex(fmt, x, M, K, codes, scales, N, NULL, 0, y, ldy, NULL, 0, flags, stream) with fewer host
+ * operations per call: it checks x, y, M and the device (the one the weight was prepared on) and launches.
+ * M above 16 returns LB_E_UNSUPPORTED (the GEMM needs lb_linear's workspace).  The handle keeps the pointers,
+ * not the memory: codes and scales must stay allocated until lb_weight_destroy.  It is the per-call path of
+ * precision.qmatmul on one QTensor (apsi/precision.py:294-299, decode products of apsi/hub_gpu.py:1305-1315),
+ * which has no separate preparation step in the reference. */
+typedef struct lb_weight lb_weight;
+int lb_weight_create(int fmt, const void* codes, const void* scales, int64_t N, int64_t K, lb_weight** out);
+int lb_weight_linear(const lb_weight* w, const void* x, int64_t M, void* y, int64_t ldy, unsigned flags,
+                     void* stream);
+int lb_weight_destroy(lb_weight* w);
+
 /* Bytes of the fixed device scratch behind lb_linear_noalloc (16 MiB + 64 KiB: the prefill path fits while
  * lb_linear_workspace_size(fmt, M, N, K) <= this, e.g. M = 2048, K = 4096). */
 #define LB_NOALLOC_SCRATCH_BYTES 16842752

@@ -84,6 +84,23 @@ def test_bad_arguments_are_rejected_before_launch(lib):
                              null) == _lib.LB_E_WORKSPACE                                       # prefill: workspace
 
 
+def test_prepared_weight_arguments_are_checked_before_the_device(lib):
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(1 << 20)
+    odd = ctypes.c_void_p((1 << 20) + 8)
+    h = ctypes.c_void_p()
+    assert lib.lb_weight_create(2, fake, fake, 4, 128, None) == _lib.LB_E_ARG                   # no out
+    assert lib.lb_weight_create(3, fake, fake, 4, 128, ctypes.byref(h)) == _lib.LB_E_UNSUPPORTED  # g32 words
+    assert lib.lb_weight_create(2, null, fake, 4, 128, ctypes.byref(h)) == _lib.LB_E_ARG
+    assert lib.lb_weight_create(2, fake, fake, 0, 128, ctypes.byref(h)) == _lib.LB_E_ARG
+    assert lib.lb_weight_create(2, fake, fake, 4, 100, ctypes.byref(h)) == _lib.LB_E_ARG        # K % 128
+    assert lib.lb_weight_create(1, fake, fake, 4, 96, ctypes.byref(h)) == _lib.LB_E_ARG         # K % 64
+    assert lib.lb_weight_create(2, odd, fake, 4, 128, ctypes.byref(h)) == _lib.LB_E_ALIGN
+    assert h.value is None
+    assert lib.lb_weight_linear(null, fake, 1, fake, 4, 0, null) == _lib.LB_E_ARG
+    assert lib.lb_weight_destroy(null) == 0
+
+
 def test_workspace_query(lib):
     n = ctypes.c_size_t(123)
     assert lib.lb_linear_workspace_size(2, 1, 4096, 4096, ctypes.byref(n)) == 0

@@ -210,6 +210,36 @@ def test_qmatmul_fast_path_matches_general_path(cuda):
     assert torch.equal(P.qmatmul(x, q), P.qmatmul(x.unsqueeze(0), q2)[0])
 
 
+def test_prepared_weight_gives_the_bits_of_linear_ex(cuda):
+    """lb_weight_linear (a weight checked once, tensor maps encoded once) against lb_linear_ex on the same
+    inputs: identical bits for int4 (box and row-copy paths) and int8, with and without static weights; M above
+    16 is refused."""
+    import torch
+    from apsi_b200 import kernels as Kn, _lib
+    from apsi_b200._lib import FMT_INT4_G128, FMT_INT8_ROW
+    g = torch.Generator(device=cuda)
+    g.manual_seed(8)
+    for fmt, N, K in [(FMT_INT4_G128, 1000, 1024), (FMT_INT4_G128, 11008, 4096), (FMT_INT4_G128, 300, 11008),
+                      (FMT_INT8_ROW, 520, 1024)]:
+        W = torch.randn((N, K), generator=g, device=cuda) * 0.02
+        codes, s16, _ = (Kn.quant_int4_g128 if fmt == FMT_INT4_G128 else Kn.quant_int8_rows)(W, want_scale32=False)
+        pw = Kn.PreparedWeight(fmt, codes.data_ptr(), s16.data_ptr(), N, K, cuda.index or 0)
+        for M in (1, 2, 3, 8, 16):
+            x = torch.randn((M, K), generator=g, device=cuda).to(torch.bfloat16)
+            ref = Kn.linear(fmt, x, codes, s16, N)
+            for static in (False, True):
+                spec = (fmt, codes.data_ptr(), s16.data_ptr(), N, K, cuda.index or 0, pw)
+                y = Kn.linear_spec(spec, x, None, static)
+                torch.cuda.synchronize()
+                assert torch.equal(y, ref), (fmt, N, K, M, static)
+        x = torch.randn((17, K), generator=g, device=cuda).to(torch.bfloat16)
+        y = torch.empty((17, N), dtype=torch.bfloat16, device=cuda)
+        rc = _lib.load().lb_weight_linear(pw.ptr, x.data_ptr(), 17, y.data_ptr(), N, 0,
+                                          torch.cuda.current_stream(cuda).cuda_stream)
+        assert rc == _lib.LB_E_UNSUPPORTED
+    assert Kn.device_errors() == 0
+
+
 def test_qmatmul_streams_settled_weights_early(cuda):
     """From a QTensor's second decode product on, precision.qmatmul launches with static weights (the weight
     stream starts before the previous kernel ends): same bits as the first, plain launch; after an in-place
