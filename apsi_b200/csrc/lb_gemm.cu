@@ -21,7 +21,9 @@
 //   warps 10..13  epilogue: tcgen05.ld -> scale / bias / accumulate -> bf16 -> global
 // Measured and not kept for narrow token tiles ([28672, 8192] at M = 64, 121 us as built): a separate code ring
 // up to 32 k-steps deep beside 4 x / A stages (131 us), and 128-byte-wide code tiles (4 k-steps of a row per
-// copy, SWIZZLE_128B, 16 k-steps in flight) beside 6 x / A stages (125 us).  With the dequantisation, the
+// copy, SWIZZLE_128B, 16 k-steps in flight) beside 6 x / A stages (125 us); and a TMA ring of activation + code
+// tiles as deep as shared memory allows (13 / 8 / 5 k-steps for 64 / 128 / 256 tokens) beside a separate ring of
+// 4 / 3 / 2 dequantised A tiles (124 us; configs[2] 196 -> 200 us).  With the dequantisation, the
 // MMAs and the activation reloads all removed the same pipeline still took 66 us: the stage round trip, not
 // the code stream, sets the pace there.
 //
