@@ -538,6 +538,9 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         if (g0 + 3 < ng) sq3 = __ldg(srow + g0 + 3);
       }
       uint32_t s2 = 0;
+      // unrolled by 8 k-steps (four scale groups): the queue's moves become register renames, so each scale
+      // load has four groups to land ([28672, 8192] at M = 64: 116.7 -> 111.4 us, the same bits)
+#pragma unroll 8
       for (int ks = k0; ks < k1; ++ks, ++it) {
         const uint32_t slot = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
