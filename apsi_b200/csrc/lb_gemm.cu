@@ -420,6 +420,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   using Cfg = GemmCfg<FMT>;
   using Sm = GemmSmem<BN>;
   constexpr int STAGES = stages(FMT, BN);
+  // Narrow token tiles (BN <= 128, six or eight stages) with 4-bit codes: two consecutive k-steps share one set
+  // of mbarriers (one wait, arrival and commit per pair of stages: half the hand-offs; their units always hold
+  // an even number of k-steps).  [28672, 8192] at M = 64: 112.0 -> 103.5 us, M = 128: 124.8 -> 120.9 us.  With
+  // the four stages of BN = 256 the pairs leave too little overlap (configs[2]: 195 -> 231 us), so not there.
+  constexpr int GS = ((FMT == 2 || FMT == 9) && BN <= 128 && STAGES % 2 == 0) ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t dyn_smem[];
   // 1024-align the carve-out (SW128 atoms)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dyn_smem) + 1023) & ~uintptr_t(1023));
@@ -474,12 +479,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         int mb, tok0, width, k0, k1, sp;
         gemm_unit(p, u, BN, mb, tok0, width, k0, k1, sp);
         for (int ks = k0; ks < k1; ++ks, ++it) {
-          const uint32_t slot = it % STAGES;
-          if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);
-          mbar_arrive_expect_tx(&full_x[slot], static_cast<uint32_t>(width) * 128u);
-          tma_load_2d(xs + slot * Sm::X_STAGE, width == BN ? &tm_x : &tm_xs, ks * BK, tok0, &full_x[slot]);
-          mbar_arrive_expect_tx(&full_w[slot], Cfg::RAW_STAGE);
-          tma_load_2d(raw + slot * Cfg::RAW_STAGE, &tm_w, ks * Cfg::RAW_ROW, mb * BM, &full_w[slot]);
+          const uint32_t slot = it % STAGES, bi = slot / GS;
+          if (slot % GS == 0) {
+            if (it >= STAGES) mbar_wait(&empty[bi], ((it / STAGES) - 1) & 1, abort_v);
+            mbar_arrive_expect_tx(&full_x[bi], static_cast<uint32_t>(GS * width) * 128u);
+            mbar_arrive_expect_tx(&full_w[bi], GS * Cfg::RAW_STAGE);
+          }
+          tma_load_2d(xs + slot * Sm::X_STAGE, width == BN ? &tm_x : &tm_xs, ks * BK, tok0, &full_x[bi]);
+          tma_load_2d(raw + slot * Cfg::RAW_STAGE, &tm_w, ks * Cfg::RAW_ROW, mb * BM, &full_w[bi]);
         }
       }
     }
@@ -496,18 +503,20 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem + b * BN;
         for (int ks = k0; ks < k1; ++ks, ++it) {
-          const uint32_t slot = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          mbar_wait(&full_x[slot], ph, abort_v);
-          mbar_wait(&a_full[slot], ph, abort_v);
-          tc_fence_after();
+          const uint32_t slot = it % STAGES, bi = slot / GS;
+          if (slot % GS == 0) {
+            const uint32_t ph = (it / STAGES) & 1;
+            mbar_wait(&full_x[bi], ph, abort_v);
+            mbar_wait(&a_full[bi], ph, abort_v);
+            tc_fence_after();
+          }
           const uint32_t xaddr = smem_u32(xs + slot * Sm::X_STAGE);
           const uint32_t aaddr = smem_u32(as + slot * A_STAGE);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             tc_mma_ss(d_tmem, smem_desc_sw128(aaddr + kk * 32), smem_desc_sw128(xaddr + kk * 32), idesc,
                       (ks > k0 || kk > 0) ? 1u : 0u);
-          tc_commit(&empty[slot]);
+          if (slot % GS == GS - 1) tc_commit(&empty[bi]);
         }
         tc_commit(&acc_full[b]);
       }
@@ -550,8 +559,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           sq0 = sq1; sq1 = sq2; sq2 = sq3;
           if (gi + 4 < ng) sq3 = __ldg(srow + gi + 4);
         }
-        mbar_wait(&full_w[slot], ph, abort_v);
-        if (it >= STAGES) mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, abort_v);   // MMA done with A
+        const uint32_t bi = slot / GS;
+        if (slot % GS == 0) {
+          mbar_wait(&full_w[bi], ph, abort_v);
+          if (it >= STAGES) mbar_wait(&empty[bi], ((it / STAGES) - 1) & 1, abort_v);   // MMA done with A
+        }
         uint32_t o[16];
         const uint32_t rbase = smem_u32(raw + slot * Cfg::RAW_STAGE) + rloc * Cfg::RAW_ROW;
         if (FMT == 2 || FMT == 9) {
@@ -587,9 +599,11 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
                        "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
                        : "memory");
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[slot]);
+        if (slot % GS == GS - 1) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor cores
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[bi]);
+        }
       }
     }
   } else {
