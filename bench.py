@@ -754,6 +754,7 @@ def run_case(case):
     gemv_down int4-g128 GEMV, M=1, [4096, 11008] (K split over a 2-CTA cluster), 12 launches
     gemv_m16  int4-g128 GEMV, M=16, [11008, 4096], 12 launches
     gemm      int4-g128 GEMM, M=2048, [12288, 4096], 4 launches (each also runs prep_x_kernel)
+    gemm_m64  int4-g128 GEMM, M=64, [28672, 8192] (configs[4]'s gate / up at M = 64), 4 launches
     quant     int4-g128 quantisation of a float32 [11008, 4096] weight, 4 launches
     decode_step  one eager decode step of the configs[3] decoder (batch 8 after a 512-token prefill), inside
               the NVTX range "decode_step" (capture it with ncu --nvtx --nvtx-include "decode_step/")"""
@@ -782,6 +783,14 @@ def run_case(case):
         y = torch.empty((GM, GN), dtype=torch.bfloat16, device=dev)
         for _ in range(4):
             Kn.linear(FMT_INT4_G128, x, p, s16, GN, out=y)
+    elif case == "gemm_m64":
+        W = torch.randn((MLP_N, MLP_K), generator=gen, device=dev) * 0.015
+        p, s16, _ = Kn.quant_int4_g128(W, want_scale32=False)
+        del W
+        x = torch.randn((64, MLP_K), generator=gen, device=dev).to(torch.bfloat16)
+        y = torch.empty((64, MLP_N), dtype=torch.bfloat16, device=dev)
+        for _ in range(4):
+            Kn.linear(FMT_INT4_G128, x, p, s16, MLP_N, out=y)
     elif case == "quant":
         W = torch.randn((N1, K1), generator=gen, device=dev) * 0.02
         for _ in range(4):
